@@ -1,0 +1,140 @@
+/*
+ * tilemix_b200 — C ABI of the B200 (sm_100a) TileMix hot path.
+ *
+ * Every entry point takes plain device pointers, element strides, sizes and a
+ * cudaStream_t passed as void*, launches asynchronously on that stream and
+ * returns an int status (TM_OK or a negative TM_ERR_* code for argument
+ * errors found on the host). The library allocates no device memory: the
+ * caller owns every buffer, including outputs and the optional device error
+ * word. Device-side wait timeouts are reported through that error word.
+ *
+ * Tensors use the reference's packed varlen layout: token-major
+ * [total_tokens, heads, head_dim] with head_dim contiguous, sequences
+ * delimited by int32 cu_seqlens[batch + 1].
+ */
+#ifndef TILEMIX_B200_H_
+#define TILEMIX_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TM_OK 0
+#define TM_ERR_NULL -1        /* a required pointer is NULL */
+#define TM_ERR_SHAPE -2       /* unsupported or inconsistent sizes */
+#define TM_ERR_ALIGN -3       /* pointer / stride alignment violated */
+#define TM_ERR_UNSUPPORTED -4 /* option outside what the kernels implement */
+#define TM_ERR_LAUNCH -5      /* CUDA launch or driver-entry-point failure */
+#define TM_ERR_TMAP -6        /* TMA descriptor encoding failed */
+
+/* Routing modes (attention/triton/tilemix.py:159-161). */
+#define TM_ROUTE_MIXED 0
+#define TM_ROUTE_FP16 1
+#define TM_ROUTE_INT8 2
+
+/*
+ * Per-block symmetric INT8 quantisation of a packed fp16 tensor.
+ * Replaces quant_per_block_int8_kernel + per_block_int8_single
+ * (attention/triton/quant_per_block_varlen.py:6-45 and :48-75).
+ *   x            fp16 [tokens, heads, dim]; strides in elements (dim stride 1)
+ *   cu_seqlens   int32 [batch+1] token offsets
+ *   cu_scale     int32 [batch+1] scale-block offsets (exclusive prefix sum of
+ *                ceil(T_b / blk))
+ *   out          int8 [tokens, heads, dim]
+ *   scale_f32    optional fp32 [sum blocks, heads] (the reference's output)
+ *   scale_f16    optional fp16 [sum blocks, heads] (the reference's host cast,
+ *                attention/triton/tilemix.py:142-155)
+ */
+int tm_quant_per_block_int8(const void* x, int64_t x_stride_tok, int64_t x_stride_head,
+                            const int32_t* cu_seqlens, const int32_t* cu_scale, int batch, int heads,
+                            int dim, int blk, int max_seqlen, float sm_scale, int8_t* out,
+                            int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32,
+                            void* scale_f16, void* stream);
+
+/*
+ * Arguments of the fused mixed-precision attention forward.
+ * Mirrors the launch of attn_fwd in launch_prequantized
+ * (attention/triton/tilemix.py:1132-1336, kernel signature :503-578).
+ */
+typedef struct tm_attn_params {
+  const void* q; /* fp16 [q_tokens, heads_q, head_dim] */
+  const void* k; /* fp16 [k_tokens, heads_k, head_dim] */
+  const void* v; /* fp16 [k_tokens, heads_k, head_dim] */
+  int64_t q_stride_tok, q_stride_head;
+  int64_t k_stride_tok, k_stride_head;
+  int64_t v_stride_tok, v_stride_head;
+  int64_t q_tokens, k_tokens;
+  void* out; /* fp16 [q_tokens, heads_q, head_dim] */
+  int64_t o_stride_tok, o_stride_head;
+
+  /* Prequantised Q (launch_prequantized). NULL => Q is quantised inside the
+   * kernel with 128-token blocks (requires blkq == 128). */
+  const int8_t* q8;
+  int64_t q8_stride_tok, q8_stride_head;
+  const void* q_scale; /* fp16 [sum ceil(Tq_b/blkq), heads_q] */
+  const int32_t* cu_q_scale;
+  /* Quantised K (required unless routing_mode == TM_ROUTE_FP16). */
+  const int8_t* k8;
+  int64_t k8_stride_tok, k8_stride_head;
+  const void* k_scale; /* fp16 [sum ceil(Tk_b/blkk), heads_k] */
+  const int32_t* cu_k_scale;
+  /* Quantised V for the INT8-V PV path (int8_use_fp16_v == 0). */
+  const int8_t* v8;
+  int64_t v8_stride_tok, v8_stride_head;
+  const void* v_scale;
+  const int32_t* cu_v_scale;
+
+  const int32_t* cu_seqlens_q; /* int32 [batch+1] */
+  const int32_t* cu_seqlens_k; /* int32 [batch+1] */
+  const uint64_t* precision_bitmask; /* uint64 [heads_k * ceil(max_seqlen_q/block_m)] */
+  const void* bias;                  /* reserved: must be NULL */
+  int64_t bias_stride[4];
+
+  int batch, heads_q, heads_k, head_dim;
+  int max_seqlen_q, max_seqlen_k;
+  int block_m, block_n, block_n_mask, blkq, blkk;
+  int causal, routing_mode, run_length, scalar_scales, int8_use_fp16_v;
+  float sm_scale;
+  int* error_flag; /* optional device int, set non-zero on a device-side timeout */
+  /* Optional device int[2], zero before the first call: work counter of the
+   * persistent kernel's dynamic scheduler (left at zero after every call).
+   * NULL = a counter inside the library, shared by all calls on a device, so
+   * calls that may overlap on the GPU must then each pass their own. */
+  int* sched_workspace;
+} tm_attn_params;
+
+/*
+ * Fused FP16/INT8 tile-routed flash-attention forward (tcgen05 + TMA + TMEM).
+ * Replaces attn_fwd (attention/triton/tilemix.py:503-951) as launched by
+ * launch_prequantized (:1132-1336). Asynchronous on `stream`. Uses the
+ * reference's softmax update rule (rescale_threshold 0).
+ */
+int tm_attn_fwd(const tm_attn_params* params, void* stream);
+
+/* Optional execution settings of tm_attn_fwd_ex (no reference counterpart:
+ * they select between equivalent B200 schedules). */
+typedef struct tm_attn_tuning {
+  /* log2-domain slack before the running softmax max is moved; 0 = the
+   * reference's rule (move on every increase). Larger values trade fp16
+   * rounding of P for fewer rescales of the output accumulator. <= 15. */
+  float rescale_threshold;
+  /* Kernel selection: 0 = automatic (the paired kernel when head_dim is 128,
+   * block_m 128 and Q is quantised in kernel, else the general kernel);
+   * 1 = always the general kernel; 2 = the persistent route-compacted kernel
+   * where the paired one would apply. */
+  int force_general;
+} tm_attn_tuning;
+
+/* tm_attn_fwd with explicit tuning (NULL = defaults of tm_attn_fwd). */
+int tm_attn_fwd_ex(const tm_attn_params* params, const tm_attn_tuning* tuning, void* stream);
+
+/* Human-readable text for a TM_* status code. */
+const char* tm_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TILEMIX_B200_H_ */

@@ -1,0 +1,34 @@
+"""GPU parity of the sm_100a per-block INT8 quantiser: bit-exact codes and scales."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention_oracle as ora
+from tests.helpers import make_qkv
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("lens,h,d,blk", [([512], 4, 64, 128), ([4096, 1000, 1], 8, 128, 64),
+                                          ([300, 129], 3, 128, 128), ([64], 1, 64, 256)])
+def test_quant_bit_exact(cuda_device, lens, h, d, blk):
+    from tilemix_b200.attention.quant_per_block_varlen import per_block_int8_single
+
+    q, _, _, cu = make_qkv(lens, h, 1, d, seed=3, outliers=2)
+    x8, xs, cus = per_block_int8_single(q.to(cuda_device), cu.to(cuda_device), max(lens), BLK=blk)
+    torch.cuda.synchronize()
+    r8, rs, rcu = ora.per_block_int8_single(q.numpy(), cu.numpy(), max(lens), BLK=blk)
+    assert np.array_equal(cus.cpu().numpy(), rcu)
+    assert np.array_equal(xs.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(x8.cpu().numpy(), r8)
+
+
+def test_quant_all_zero_block(cuda_device):
+    from tilemix_b200.attention.quant_per_block_varlen import per_block_int8_single
+
+    x = torch.zeros((128, 2, 64), dtype=torch.float16)
+    x[:, 1] = 1.0
+    cu = torch.tensor([0, 128], dtype=torch.int32)
+    x8, xs, _ = per_block_int8_single(x.to(cuda_device), cu.to(cuda_device), 128, BLK=128)
+    assert float(xs[0, 0]) == 0.0 and int(x8[:, 0].abs().max()) == 0
+    assert int(x8[:, 1].min()) == 127

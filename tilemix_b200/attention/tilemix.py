@@ -1,0 +1,401 @@
+"""Host launch layer of the B200 TileMix attention (drop-in for the reference's
+``attention/triton/tilemix.py`` host functions).
+
+Public functions keep the reference's names, arguments, validation errors and
+return values:
+
+  quantize_qkv_for_tilemix   tilemix.py:45-107
+  quantize_qk_for_tilemix    tilemix.py:110-156
+  classify_bitmask_routing   tilemix.py:968-1014
+  launch_prequantized        tilemix.py:1132-1336
+  tilemix_attention_with_quant  tilemix.py:1340-1447
+
+Underneath, every launch goes through the C ABI ``tm_attn_fwd_ex`` of
+``libtilemix_b200.so`` (hand-written tcgen05/TMA kernel for sm_100a). There is
+no Triton, no autotuner and no CPU fallback. Differences in mechanism, not in
+results:
+  * ``tilemix_attention_with_quant`` quantises Q inside the attention kernel
+    (the 128-row CTA tile is exactly one BLKQ=128 block), so only K (and V for
+    the INT8-V path) goes through the standalone quantiser;
+  * ``run_length`` and ``int8_cache_ca`` only changed loop structure / cache
+    hints in the reference and do not change results; they are accepted and
+    have no effect;
+  * the online softmax is updated per 64-key tile for any ``block_n`` that is a
+    multiple of 64 (the reference updates once per ``block_n`` tile); keys the
+    reference visits beyond the causal limit are fully masked either way.
+Environment: ``TILEMIX_B200_RESCALE_THRESHOLD`` (log2 units, default 8): the
+running softmax max is moved only when a tile max exceeds it by more than this
+amount; 0 reproduces the reference's update-on-every-increase exactly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Literal, Optional
+
+import torch
+
+from tilemix_b200._lib import TmAttnParams, TmAttnTuning, check, lib
+from tilemix_b200.attention.quant_per_block_varlen import (
+    _launch_quant,
+    _scale_offsets,
+    per_block_int8 as quant_per_block_int8,
+    per_block_int8_single,
+)
+
+ROUTING_MODE_MIXED = 0
+ROUTING_MODE_FP16 = 1
+ROUTING_MODE_INT8 = 2
+RoutingMode = Literal["auto", "mixed", "fp16", "int8"]
+
+_ERROR_WORDS: dict[int, torch.Tensor] = {}
+_SCHED_WORDS: dict[int, torch.Tensor] = {}
+
+
+def _sched_word(device: torch.device) -> torch.Tensor:
+    """Per-device scheduler counters of the persistent kernel (left at zero by every launch)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _SCHED_WORDS.get(idx)
+    if w is None:
+        w = torch.zeros(2, dtype=torch.int32, device=torch.device("cuda", idx))
+        _SCHED_WORDS[idx] = w
+    return w
+
+
+def _error_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _ERROR_WORDS.get(idx)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _ERROR_WORDS[idx] = w
+    return w
+
+
+def device_error_code(device: Optional[torch.device] = None, reset: bool = True) -> int:
+    """Read (and optionally clear) the device error word of the attention kernel.
+
+    Non-zero means a bounded wait inside the kernel timed out (codes in
+    csrc/common.cuh). Synchronises the device.
+    """
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    w = _error_word(device)
+    code = int(w.item())
+    if reset and code:
+        w.zero_()
+    return code
+
+
+def rescale_threshold() -> float:
+    return float(os.environ.get("TILEMIX_B200_RESCALE_THRESHOLD", "8"))
+
+
+def _scale_dtype(dtype: torch.dtype) -> torch.dtype:
+    if dtype == torch.float16:
+        return torch.float16
+    if dtype == torch.bfloat16:
+        return torch.bfloat16
+    return torch.float32
+
+
+@torch.no_grad()
+def quantize_qkv_for_tilemix(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, BLKQ: int = 128,
+                             BLKK: int = 64, sm_scale: float = None):
+    """Quantise Q, K and V per block (tilemix.py:45-107)."""
+    q8, q_scale_blocks, k8, k_scale_blocks, cu_q_scale, cu_k_scale = quant_per_block_int8(
+        q, k, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, BLKQ=BLKQ, BLKK=BLKK, sm_scale=1.0)
+    v8, v_scale_blocks, cu_v_scale = per_block_int8_single(v, cu_seqlens_k, max_seqlen_k, BLK=BLKK, sm_scale=1.0)
+    sd = _scale_dtype(q.dtype)
+    return (q8, q_scale_blocks.to(dtype=sd).contiguous(), cu_q_scale.to(dtype=torch.int32).contiguous(),
+            k8, k_scale_blocks.to(dtype=sd).contiguous(), cu_k_scale.to(dtype=torch.int32).contiguous(),
+            v8, v_scale_blocks.to(dtype=sd).contiguous(), cu_v_scale.to(dtype=torch.int32).contiguous())
+
+
+@torch.no_grad()
+def quantize_qk_for_tilemix(q, k, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, BLKQ: int = 128,
+                            BLKK: int = 64, sm_scale: float = None):
+    """Quantise Q and K per block (tilemix.py:110-156)."""
+    q8, q_scale_blocks, k8, k_scale_blocks, cu_q_scale, cu_k_scale = quant_per_block_int8(
+        q, k, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, BLKQ=BLKQ, BLKK=BLKK, sm_scale=1.0)
+    sd = _scale_dtype(q.dtype)
+    return (q8.contiguous(), q_scale_blocks.to(dtype=sd).contiguous(), cu_q_scale.to(dtype=torch.int32).contiguous(),
+            k8.contiguous(), k_scale_blocks.to(dtype=sd).contiguous(), cu_k_scale.to(dtype=torch.int32).contiguous())
+
+
+def _routing_mode_code(mode: str) -> int:
+    normalized = mode.strip().lower()
+    codes = {"mixed": ROUTING_MODE_MIXED, "fp16": ROUTING_MODE_FP16, "int8": ROUTING_MODE_INT8}
+    if normalized not in codes:
+        raise ValueError(f"routing_mode must be one of {tuple(codes)}, got {mode!r}")
+    return codes[normalized]
+
+
+def classify_bitmask_routing(precision_bitmask: torch.Tensor, *, seqlen_q: int, seqlen_k: int, block_m: int,
+                             block_n: int, block_n_mask: int, causal: bool) -> Literal["mixed", "fp16", "int8"]:
+    """Decide whether a map routes everything to one format (tilemix.py:968-1014)."""
+    if block_n_mask % block_n != 0:
+        raise ValueError("block_n_mask must be a multiple of block_n")
+    m_blocks = (seqlen_q + block_m - 1) // block_m
+    compute_blocks = (seqlen_k + block_n - 1) // block_n
+    mask_group = block_n_mask // block_n
+    host_masks = precision_bitmask.detach().reshape(-1).cpu().tolist()
+    if len(host_masks) == 0 or len(host_masks) % m_blocks:
+        raise ValueError("precision_bitmask has an invalid row count")
+    all_fp16 = True
+    all_int8 = True
+    for row, raw_mask in enumerate(host_masks):
+        query_block = row % m_blocks
+        row_blocks = compute_blocks
+        if causal:
+            numerator = (query_block + 1) * block_m + seqlen_k - seqlen_q
+            row_blocks = max(0, min(compute_blocks, (numerator + block_n - 1) // block_n))
+        route_blocks = (row_blocks + mask_group - 1) // mask_group
+        valid_mask = (1 << route_blocks) - 1 if route_blocks else 0
+        routed = (int(raw_mask) & ((1 << 64) - 1)) & valid_mask
+        all_fp16 &= routed == 0
+        all_int8 &= routed == valid_mask
+        if not all_fp16 and not all_int8:
+            return "mixed"
+    if all_fp16:
+        return "fp16"
+    if all_int8:
+        return "int8"
+    return "mixed"
+
+
+def _ptr(t: Optional[torch.Tensor]) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
+
+
+def _launch(q, k, v, o, cu_q, cu_k, bitmask, max_q, max_k, *, q8=None, sq=None, cuqs=None, k8=None, sk=None,
+            cuks=None, block_m, block_n, block_n_mask, BLKQ, BLKK, causal, sm_scale, mode_code, scalar_scales,
+            int8_use_fp16_v, threshold=None) -> None:
+    p = TmAttnParams()
+    p.q, p.k, p.v = _ptr(q), _ptr(k), _ptr(v)
+    p.q_stride_tok, p.q_stride_head = q.stride(0), q.stride(1)
+    p.k_stride_tok, p.k_stride_head = k.stride(0), k.stride(1)
+    p.v_stride_tok, p.v_stride_head = v.stride(0), v.stride(1)
+    p.q_tokens, p.k_tokens = q.shape[0], k.shape[0]
+    p.out = _ptr(o)
+    p.o_stride_tok, p.o_stride_head = o.stride(0), o.stride(1)
+    if q8 is not None:
+        p.q8 = _ptr(q8)
+        p.q8_stride_tok, p.q8_stride_head = q8.stride(0), q8.stride(1)
+        p.q_scale, p.cu_q_scale = _ptr(sq), _ptr(cuqs)
+    if k8 is not None:
+        p.k8 = _ptr(k8)
+        p.k8_stride_tok, p.k8_stride_head = k8.stride(0), k8.stride(1)
+        p.k_scale, p.cu_k_scale = _ptr(sk), _ptr(cuks)
+    p.cu_seqlens_q, p.cu_seqlens_k = _ptr(cu_q), _ptr(cu_k)
+    p.precision_bitmask = _ptr(bitmask)
+    p.batch = cu_q.numel() - 1
+    p.heads_q, p.heads_k, p.head_dim = q.shape[1], k.shape[1], q.shape[2]
+    p.max_seqlen_q, p.max_seqlen_k = int(max_q), int(max_k)
+    p.block_m, p.block_n, p.block_n_mask = block_m, block_n, block_n_mask
+    p.blkq, p.blkk = BLKQ, BLKK
+    p.causal = int(bool(causal))
+    p.routing_mode = mode_code
+    p.scalar_scales = int(bool(scalar_scales))
+    p.int8_use_fp16_v = int(bool(int8_use_fp16_v))
+    p.sm_scale = float(sm_scale)
+    p.error_flag = _ptr(_error_word(q.device))
+    p.sched_workspace = _ptr(_sched_word(q.device))
+    tune = TmAttnTuning()
+    tune.rescale_threshold = rescale_threshold() if threshold is None else float(threshold)
+    tune.force_general = {"general": 1, "persistent": 2}.get(
+        os.environ.get("TILEMIX_B200_KERNEL", "").strip().lower(), 0)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    with torch.cuda.device(q.device):
+        rc = lib().tm_attn_fwd_ex(ctypes.byref(p), ctypes.byref(tune), ctypes.c_void_p(stream))
+    check(rc, "tm_attn_fwd")
+
+
+def _check_kernel_support(q, block_m, block_n, BLKK, int8_path: bool, int8_use_fp16_v: bool, bias) -> None:
+    if q.dtype != torch.float16:
+        raise TypeError("the sm_100a TileMix kernel computes in fp16; q, k and v must be torch.float16")
+    if q.shape[-1] not in (64, 128):
+        raise ValueError("the sm_100a TileMix kernel supports head_dim 64 and 128")
+    if block_m not in (64, 128) or block_n % 64 != 0:
+        raise ValueError("the sm_100a TileMix kernel supports block_m in (64, 128) and block_n a multiple of 64")
+    if int8_path and BLKK % 64 != 0:
+        raise ValueError("the sm_100a TileMix kernel needs BLKK to be a multiple of 64")
+    if bias is not None:
+        raise NotImplementedError("additive bias is not implemented by the sm_100a TileMix kernel")
+    if int8_path and not int8_use_fp16_v:
+        raise NotImplementedError("the INT8-V PV path (int8_use_fp16_v=False) is not implemented by the "
+                                  "sm_100a TileMix kernel; pass int8_use_fp16_v=True")
+
+
+@torch.no_grad()
+def launch_prequantized(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q: int, max_seqlens_k: int,
+                        precision_bitmask, *, q8, k8, v8, sQ_blocks, sK_blocks, sV_blocks, cu_q_scale, cu_k_scale,
+                        cu_v_scale, block_m: int = 128, block_n: int = 64, block_n_mask: Optional[int] = None,
+                        BLKQ: int = 128, BLKK: int = 64, causal: bool = False, sm_scale: Optional[float] = None,
+                        bias: Optional[torch.Tensor] = None, o: Optional[torch.Tensor] = None,
+                        routing_mode: RoutingMode = "auto", run_length: bool = False, scalar_scales: bool = True,
+                        int8_cache_ca: bool = False, int8_use_fp16_v: bool = False):
+    """Launch the attention kernel on prequantised Q/K(/V) (tilemix.py:1132-1336)."""
+    if not q.is_cuda:
+        raise RuntimeError("TileMix is a CUDA-only kernel")
+    if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
+        raise ValueError("expected flattened [tokens, heads, dim] tensors")
+    if k.shape != v.shape or q.shape[-1] != k.shape[-1]:
+        raise ValueError("K/V shapes and Q/K/V head dimensions must match")
+    if q.shape[1] % k.shape[1] != 0:
+        raise ValueError("Q heads must be divisible by KV heads")
+    if q.device != k.device or q.device != v.device:
+        raise ValueError("q, k, and v must share one CUDA device")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise TypeError("q, k, and v must share one dtype")
+    if max_seqlens_q != max_seqlens_k:
+        raise ValueError("packed routing currently requires equal Q/K lengths")
+    if block_n_mask is None:
+        block_n_mask = block_n
+    if block_n_mask % block_n:
+        raise ValueError("block_n_mask must be a multiple of block_n")
+    if (max_seqlens_k + block_n_mask - 1) // block_n_mask > 64:
+        raise ValueError("packed routing exceeds 64 mask blocks")
+    if scalar_scales and (block_m != BLKQ or block_n != BLKK):
+        raise ValueError("scalar_scales requires block_m == BLKQ and block_n == BLKK")
+    expected_rows = k.shape[1] * ((max_seqlens_q + block_m - 1) // block_m)
+    if precision_bitmask.dtype != torch.uint64:
+        raise TypeError("precision_bitmask must be torch.uint64")
+    if precision_bitmask.numel() != expected_rows:
+        raise ValueError(f"precision_bitmask has {precision_bitmask.numel()} rows, expected {expected_rows}")
+    normalized_mode = routing_mode.strip().lower()
+    if normalized_mode == "auto":
+        normalized_mode = classify_bitmask_routing(precision_bitmask, seqlen_q=max_seqlens_q,
+                                                   seqlen_k=max_seqlens_k, block_m=block_m, block_n=block_n,
+                                                   block_n_mask=block_n_mask, causal=causal)
+    mode_code = _routing_mode_code(normalized_mode)
+    quant_tensors = (q8, k8, v8, sQ_blocks, sK_blocks, sV_blocks, cu_q_scale, cu_k_scale, cu_v_scale)
+    if any(t.device != q.device for t in quant_tensors):
+        raise ValueError("all quantization tensors must share q.device")
+    if q8.dtype != torch.int8 or k8.dtype != torch.int8:
+        raise TypeError("q8 and k8 must be torch.int8")
+    if v8.dtype != torch.int8:
+        raise TypeError("v8 must be torch.int8")
+    if sm_scale is None:
+        sm_scale = q.shape[-1] ** -0.5
+    if o is None:
+        o = torch.empty_like(q)
+    cu_seqlens_q = cu_seqlens_q.to(device=q.device, dtype=torch.int32).contiguous()
+    cu_seqlens_k = cu_seqlens_k.to(device=q.device, dtype=torch.int32).contiguous()
+    precision_bitmask = precision_bitmask.to(device=q.device, dtype=torch.uint64).contiguous()
+    head_dim = q.shape[-1]
+    padded_head_dim = max(32, 1 << (head_dim - 1).bit_length())
+    padded_head_dim = ((padded_head_dim + 31) // 32) * 32
+    if padded_head_dim > 128:
+        raise ValueError("head dimension must be <= 128")
+    int8_path = mode_code != ROUTING_MODE_FP16
+    _check_kernel_support(q, block_m, block_n, BLKK, int8_path, int8_use_fp16_v, bias)
+    kw = {}
+    if int8_path:
+        kw = dict(q8=q8, sq=sQ_blocks.to(torch.float16).contiguous(), cuqs=cu_q_scale.to(torch.int32).contiguous(),
+                  k8=k8, sk=sK_blocks.to(torch.float16).contiguous(), cuks=cu_k_scale.to(torch.int32).contiguous())
+    _launch(q, k, v, o, cu_seqlens_q, cu_seqlens_k, precision_bitmask, max_seqlens_q, max_seqlens_k,
+            block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, BLKQ=BLKQ, BLKK=BLKK, causal=causal,
+            sm_scale=sm_scale, mode_code=mode_code, scalar_scales=scalar_scales,
+            int8_use_fp16_v=int8_use_fp16_v, **kw)
+    return o, normalized_mode
+
+
+def _quantize_k(k, cu_seqlens_k, max_seqlen_k, BLKK, equal_len: Optional[int] = None):
+    """K codes + fp16 block scales + int32 block offsets, without a host sync for equal lengths."""
+    batch = cu_seqlens_k.numel() - 1
+    if equal_len is not None:
+        nblk = (equal_len + BLKK - 1) // BLKK
+        cu_scale_i32 = torch.arange(0, (batch + 1) * nblk, nblk, device=k.device, dtype=torch.int32)
+        n_rows = batch * nblk
+    else:
+        cu_scale, cu_scale_i32 = _scale_offsets(cu_seqlens_k, BLKK, max_seqlen_k)
+        n_rows = int(cu_scale[-1].item())
+    k8 = torch.empty(k.shape, dtype=torch.int8, device=k.device)
+    sk16 = torch.empty((n_rows, k.shape[1]), dtype=torch.float16, device=k.device)
+    cu_i32 = cu_seqlens_k.to(device=k.device, dtype=torch.int32).contiguous()
+    _launch_quant(k, cu_i32, cu_scale_i32, max_seqlen_k, BLKK, 1.0, k8, None, sk16)
+    return k8, sk16, cu_scale_i32
+
+
+@torch.no_grad()
+def _attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q, max_seqlens_k, precision_bitmask, *,
+                       block_m, block_n, block_n_mask, BLKQ, BLKK, causal, sm_scale, mode: str, scalar_scales,
+                       int8_use_fp16_v, bias=None, equal_len: Optional[int] = None, o=None, threshold=None):
+    mode_code = _routing_mode_code(mode)
+    int8_path = mode_code != ROUTING_MODE_FP16
+    _check_kernel_support(q, block_m, block_n, BLKK, int8_path, int8_use_fp16_v, bias)
+    if sm_scale is None:
+        sm_scale = q.shape[-1] ** -0.5
+    if o is None:
+        o = torch.empty_like(q)
+    cu_q = cu_seqlens_q.to(device=q.device, dtype=torch.int32).contiguous()
+    cu_k = cu_seqlens_k.to(device=q.device, dtype=torch.int32).contiguous()
+    bm = precision_bitmask.to(device=q.device, dtype=torch.uint64).contiguous()
+    kw = {}
+    if int8_path:
+        k8, sk16, cuks = _quantize_k(k, cu_k, max_seqlens_k, BLKK, equal_len)
+        kw = dict(k8=k8, sk=sk16, cuks=cuks)
+        if BLKQ != 128:
+            q8, sq, cuq = per_block_int8_single(q, cu_q, max_seqlens_q, BLK=BLKQ, sm_scale=1.0)
+            kw.update(q8=q8, sq=sq.to(torch.float16).contiguous(), cuqs=cuq.to(torch.int32).contiguous())
+    _launch(q, k, v, o, cu_q, cu_k, bm, max_seqlens_q, max_seqlens_k, block_m=block_m, block_n=block_n,
+            block_n_mask=block_n_mask, BLKQ=BLKQ, BLKK=BLKK, causal=causal, sm_scale=sm_scale,
+            mode_code=mode_code, scalar_scales=scalar_scales, int8_use_fp16_v=int8_use_fp16_v,
+            threshold=threshold, **kw)
+    return o
+
+
+@torch.no_grad()
+def tilemix_attention_with_quant(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q: int, max_seqlens_k: int,
+                                 precision_bitmask, *, block_m: int = 128, block_n: int = 64,
+                                 block_n_mask: Optional[int] = None, BLKQ: int = 128, BLKK: int = 64,
+                                 causal: bool = False, sm_scale: Optional[float] = None,
+                                 bias: Optional[torch.Tensor] = None, routing_mode: RoutingMode = "auto",
+                                 run_length: bool = False, scalar_scales: bool = True, int8_cache_ca: bool = False,
+                                 int8_use_fp16_v: bool = False):
+    """Quantise and run the routed attention (tilemix.py:1340-1447). Returns (out, mode)."""
+    if block_n_mask is None:
+        block_n_mask = block_n
+    normalized_mode = routing_mode.strip().lower()
+    if normalized_mode == "auto":
+        normalized_mode = classify_bitmask_routing(precision_bitmask, seqlen_q=max_seqlens_q,
+                                                   seqlen_k=max_seqlens_k, block_m=block_m, block_n=block_n,
+                                                   block_n_mask=block_n_mask, causal=causal)
+    _validate(q, k, v, max_seqlens_q, max_seqlens_k, precision_bitmask, block_m, block_n, block_n_mask, BLKQ,
+              BLKK, scalar_scales)
+    _routing_mode_code(normalized_mode)
+    o = _attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q, max_seqlens_k, precision_bitmask,
+                           block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, BLKQ=BLKQ, BLKK=BLKK,
+                           causal=causal, sm_scale=sm_scale, mode=normalized_mode, scalar_scales=scalar_scales,
+                           int8_use_fp16_v=int8_use_fp16_v, bias=bias)
+    return o, normalized_mode
+
+
+def _validate(q, k, v, max_q, max_k, bitmask, block_m, block_n, block_n_mask, BLKQ, BLKK, scalar_scales):
+    """The argument checks launch_prequantized performs (tilemix.py:1167-1201)."""
+    if not q.is_cuda:
+        raise RuntimeError("TileMix is a CUDA-only kernel")
+    if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
+        raise ValueError("expected flattened [tokens, heads, dim] tensors")
+    if k.shape != v.shape or q.shape[-1] != k.shape[-1]:
+        raise ValueError("K/V shapes and Q/K/V head dimensions must match")
+    if q.shape[1] % k.shape[1] != 0:
+        raise ValueError("Q heads must be divisible by KV heads")
+    if q.device != k.device or q.device != v.device:
+        raise ValueError("q, k, and v must share one CUDA device")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise TypeError("q, k, and v must share one dtype")
+    if max_q != max_k:
+        raise ValueError("packed routing currently requires equal Q/K lengths")
+    if block_n_mask % block_n:
+        raise ValueError("block_n_mask must be a multiple of block_n")
+    if (max_k + block_n_mask - 1) // block_n_mask > 64:
+        raise ValueError("packed routing exceeds 64 mask blocks")
+    if scalar_scales and (block_m != BLKQ or block_n != BLKK):
+        raise ValueError("scalar_scales requires block_m == BLKQ and block_n == BLKK")
+    expected_rows = k.shape[1] * ((max_q + block_m - 1) // block_m)
+    if bitmask.dtype != torch.uint64:
+        raise TypeError("precision_bitmask must be torch.uint64")
+    if bitmask.numel() != expected_rows:
+        raise ValueError(f"precision_bitmask has {bitmask.numel()} rows, expected {expected_rows}")
+    if q.shape[-1] > 128:
+        raise ValueError("head dimension must be <= 128")

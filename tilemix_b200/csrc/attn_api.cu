@@ -1,0 +1,186 @@
+// C ABI of the attention forward: argument checks, TMA descriptor encoding and
+// dispatch between the two sm_100a kernels:
+//   * paired  (attn_fwd_paired.cu): head_dim 128, block_m 128, Q quantised in
+//     kernel (or FP16-only routing) -- the model / tilemix_attention_with_quant path;
+//   * persistent (attn_fwd_persistent.cu): same shapes, route-compacted
+//     persistent schedule; selected explicitly (tuning.force_general == 2);
+//   * general (attn_fwd_general.cu): everything else the API accepts (block_m 64,
+//     head_dim 64, prequantised Q from launch_prequantized).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "attn_common.cuh"
+#include "tilemix_b200.h"
+
+namespace tilemix {
+
+int launch_attn_general(const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v, const AttnArgs& a,
+                        int tiles, int heads_q, int batch, cudaStream_t stream);
+int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
+                       const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
+int launch_attn_persistent(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
+                           const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D map over a packed [tokens, heads, dim] tensor: dims {dim, heads, tokens}; box {box_inner, 1, box_rows}.
+static int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, int dim, int heads,
+                    int64_t tokens, int64_t stride_head, int64_t stride_tok, int box_inner,
+                    CUtensorMapSwizzle swz, int box_rows = 64) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return TM_ERR_LAUNCH;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(tokens)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride_head * elem_bytes),
+                           static_cast<cuuint64_t>(stride_tok * elem_bytes)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_inner), 1u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TM_OK : TM_ERR_TMAP;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace tilemix
+
+extern "C" int tm_attn_fwd(const tm_attn_params* p, void* stream) { return tm_attn_fwd_ex(p, nullptr, stream); }
+
+extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tuning, void* stream) {
+  const float rescale_threshold = tuning ? tuning->rescale_threshold : 0.f;
+  const int kernel_choice = tuning ? tuning->force_general : 0;  // 0 auto, 1 general, 2 persistent
+  const int force_general = kernel_choice == 1;
+  using namespace tilemix;
+  if (p == nullptr) return TM_ERR_NULL;
+  if (p->q == nullptr || p->k == nullptr || p->v == nullptr || p->out == nullptr || p->cu_seqlens_q == nullptr ||
+      p->cu_seqlens_k == nullptr)
+    return TM_ERR_NULL;
+  if (p->batch < 0 || p->heads_q <= 0 || p->heads_k <= 0 || p->heads_q % p->heads_k != 0) return TM_ERR_SHAPE;
+  if (p->head_dim != 64 && p->head_dim != 128) return TM_ERR_UNSUPPORTED;
+  if (p->block_m != 64 && p->block_m != 128) return TM_ERR_UNSUPPORTED;
+  if (p->block_n <= 0 || p->block_n % 64 != 0) return TM_ERR_UNSUPPORTED;
+  if (p->block_n_mask <= 0 || p->block_n_mask % p->block_n != 0) return TM_ERR_SHAPE;
+  if (p->routing_mode < 0 || p->routing_mode > 2) return TM_ERR_SHAPE;
+  if (p->bias != nullptr) return TM_ERR_UNSUPPORTED;
+  if (p->routing_mode != TM_ROUTE_FP16 && !p->int8_use_fp16_v) return TM_ERR_UNSUPPORTED;
+  if (rescale_threshold < 0.f || rescale_threshold > 15.f) return TM_ERR_SHAPE;
+  if (p->routing_mode == TM_ROUTE_MIXED && p->precision_bitmask == nullptr) return TM_ERR_NULL;
+  const bool need_int8 = p->routing_mode != TM_ROUTE_FP16;
+  const bool fuse_q = need_int8 && p->q8 == nullptr;
+  if (need_int8) {
+    if (p->k8 == nullptr || p->k_scale == nullptr || p->cu_k_scale == nullptr) return TM_ERR_NULL;
+    if (p->blkk <= 0 || p->blkk % 64 != 0) return TM_ERR_UNSUPPORTED;
+    if (fuse_q && p->blkq != 128) return TM_ERR_UNSUPPORTED;
+    if (!fuse_q && (p->q_scale == nullptr || p->cu_q_scale == nullptr || p->blkq <= 0)) return TM_ERR_NULL;
+  }
+  if (p->batch == 0 || p->max_seqlen_q == 0) return TM_OK;
+  if (p->max_seqlen_k > 0 && (p->max_seqlen_k + p->block_n_mask - 1) / p->block_n_mask > 64) return TM_ERR_SHAPE;
+  // Alignment: 16-byte rows for TMA and vector loads/stores.
+  const int64_t strides_fp16[] = {p->q_stride_tok, p->q_stride_head, p->k_stride_tok, p->k_stride_head,
+                                  p->v_stride_tok, p->v_stride_head, p->o_stride_tok, p->o_stride_head};
+  for (int64_t s : strides_fp16)
+    if (s % 8 != 0) return TM_ERR_ALIGN;
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->out)) return TM_ERR_ALIGN;
+  if (need_int8) {
+    if (!aligned16(p->k8) || p->k8_stride_tok % 16 != 0 || p->k8_stride_head % 16 != 0) return TM_ERR_ALIGN;
+    if (!fuse_q && (!aligned16(p->q8) || p->q8_stride_tok % 16 != 0 || p->q8_stride_head % 16 != 0))
+      return TM_ERR_ALIGN;
+  }
+  const int D = p->head_dim;
+  CUtensorMap m_k16, m_k8, m_v;
+  int rc = make_map(&m_k16, p->k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, p->heads_k, p->k_tokens, p->k_stride_head,
+                    p->k_stride_tok, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != TM_OK) return rc;
+  rc = make_map(&m_v, p->v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, p->heads_k, p->k_tokens, p->v_stride_head,
+                p->v_stride_tok, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != TM_OK) return rc;
+  if (need_int8) {
+    rc = make_map(&m_k8, p->k8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, p->heads_k, p->k_tokens, p->k8_stride_head,
+                  p->k8_stride_tok, D, D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc != TM_OK) return rc;
+  } else {
+    m_k8 = m_k16;  // never read
+  }
+
+  AttnArgs a;
+  a.q = static_cast<const __half*>(p->q);
+  a.q_st = p->q_stride_tok;
+  a.q_sh = p->q_stride_head;
+  a.out = static_cast<__half*>(p->out);
+  a.o_st = p->o_stride_tok;
+  a.o_sh = p->o_stride_head;
+  a.q8 = p->q8;
+  a.q8_st = p->q8_stride_tok;
+  a.q8_sh = p->q8_stride_head;
+  a.q_scale = static_cast<const __half*>(p->q_scale);
+  a.cu_qs = p->cu_q_scale;
+  a.k_scale = static_cast<const __half*>(p->k_scale);
+  a.cu_ks = p->cu_k_scale;
+  a.cu_q = p->cu_seqlens_q;
+  a.cu_k = p->cu_seqlens_k;
+  a.bitmask = p->precision_bitmask;
+  a.HQ = p->heads_q;
+  a.HK = p->heads_k;
+  a.group = p->heads_q / p->heads_k;
+  a.D = D;
+  a.block_m = p->block_m;
+  a.block_n_mask = p->block_n_mask;
+  a.blkq = p->blkq;
+  a.blkk = p->blkk;
+  a.causal = p->causal;
+  a.mode = p->routing_mode;
+  a.fuse_q = fuse_q ? 1 : 0;
+  // qk_scale = fp32(sm_scale) * fp32(log2 e), as the reference evaluates it (:639).
+  a.qk_scale = p->sm_scale * 1.44269502162933349609375f;
+  a.rescale_threshold = rescale_threshold;
+  a.err = p->error_flag;
+  a.sched = p->sched_workspace;
+
+  a.pair_heads = (a.group % 2 == 0) ? 1 : 0;
+  if (p->heads_q > 65535 || p->batch > 65535) return TM_ERR_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool paired_ok = !force_general && D == 128 && p->block_m == 128 && (fuse_q || !need_int8);
+  if (paired_ok) {
+    CUtensorMap m_q;
+    rc = make_map(&m_q, p->q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, p->heads_q, p->q_tokens, p->q_stride_head,
+                  p->q_stride_tok, 64, CU_TENSOR_MAP_SWIZZLE_128B, 128);
+    if (rc != TM_OK) return rc;
+    if (kernel_choice == 2) return launch_attn_persistent(m_q, m_k16, m_k8, m_v, a, p->batch, p->max_seqlen_q, st);
+    return launch_attn_paired(m_q, m_k16, m_k8, m_v, a, p->batch, p->max_seqlen_q, st);
+  }
+  const int tiles = (p->max_seqlen_q + 127) / 128;
+  return launch_attn_general(m_k16, m_k8, m_v, a, tiles, p->heads_q, p->batch, st);
+}
+
+extern "C" const char* tm_status_string(int status) {
+  switch (status) {
+    case TM_OK:
+      return "ok";
+    case TM_ERR_NULL:
+      return "a required pointer is NULL";
+    case TM_ERR_SHAPE:
+      return "unsupported or inconsistent sizes";
+    case TM_ERR_ALIGN:
+      return "pointer or stride alignment violated (16-byte rows required)";
+    case TM_ERR_UNSUPPORTED:
+      return "option not implemented by the sm_100a kernels";
+    case TM_ERR_LAUNCH:
+      return "CUDA launch failed";
+    case TM_ERR_TMAP:
+      return "TMA descriptor encoding failed";
+    default:
+      return "unknown status";
+  }
+}

@@ -1,0 +1,219 @@
+// Pieces shared by the two attention kernels (general and paired).
+//
+// The per-tile softmax below is the reference's _softmax_prefix_update
+// (attention/triton/tilemix.py:179-207) applied to one 64-key score tile held
+// in tensor memory, for the one query row owned by the calling thread:
+//   qk   = fp16(S)                                (FP16 route, fp32 accumulated S)
+//        = fp16(f32(S_i32) * score_scale)         (INT8 route, :401-404)
+//   keys at or beyond `lim` are masked to -inf    (causal / length, :256-262)
+//   p    = fp16(exp2(f32(qk) - m))                (:195-199)
+//   l   += sum exp2(f32(qk) - m)                 (:200, :206; summed before the
+//          fp16 rounding of p, a difference below fp16 resolution)
+// where m is the row's reference maximum. With threshold 0 it is updated on
+// every increase (the reference's rule); with threshold t > 0 it only moves
+// when the tile max exceeds it by more than t (log2 units), which bounds
+// p by 2^t and makes rescaling of the output accumulator rare.
+#pragma once
+
+#include "common.cuh"
+
+namespace tilemix {
+
+constexpr int kKeys = 64;  // keys per hardware score tile
+
+struct AttnArgs {
+  const __half* q;
+  int64_t q_st, q_sh;
+  __half* out;
+  int64_t o_st, o_sh;
+  const int8_t* q8;
+  int64_t q8_st, q8_sh;
+  const __half* q_scale;
+  const int32_t* cu_qs;
+  const __half* k_scale;
+  const int32_t* cu_ks;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  const uint64_t* bitmask;
+  int HQ, HK, group, D;
+  int block_m, block_n_mask, blkq, blkk;
+  int causal, mode, fuse_q;
+  int pair_heads;  // paired kernel: 1 = CTA holds two heads of one KV group, 0 = two m-tiles of one head
+  float qk_scale;
+  float rescale_threshold;
+  int* err;
+  int* sched;  // dynamic scheduler counters (int[2]) of the persistent kernel
+};
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  tmem_st16(taddr, r);
+  tmem_st16(taddr + 16, r + 16);
+}
+
+// Exact int32 -> fp32 for |x| < 2^22 without the conversion pipe: the bit
+// pattern of 1.5*2^23 plus x is the float 1.5*2^23 + x; subtracting 1.5*2^23
+// is exact. INT8 scores are bounded by 128 * 127 * 127 < 2^21.
+__device__ __forceinline__ float i2f_exact(uint32_t x) { return __uint_as_float(x + 0x4B400000u) - 12582912.0f; }
+
+__device__ __forceinline__ uint64_t f32x2_pack(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ float2 f32x2_unpack(uint64_t v) {
+  return make_float2(__uint_as_float(static_cast<uint32_t>(v)), __uint_as_float(static_cast<uint32_t>(v >> 32)));
+}
+__device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// One softmax step over a 64-key tile for this thread's row.
+//   taddr     TMEM address (lane and first column) of the 64 score columns
+//   kind      0: fp32 scores (FP16 route)   1: int32 scores (INT8 route)
+//   ss        fp32 value of the fp16 score scale (INT8 route)
+//   lim       number of valid keys of this row in the tile (>= 64: none masked)
+//   thr       rescale threshold (0 = reference rule)
+// Outputs the packed fp16 P row in p[32]; o_scale/need_rescale say whether the
+// O accumulator row has to be multiplied by o_scale before this P is added.
+__device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss, int lim, float thr,
+                                             float& m_used, float& l, uint32_t (&p)[32], float& o_scale,
+                                             bool& need_rescale) {
+  uint32_t s0[32], s1[32];
+  tmem_ld32(taddr, s0);
+  tmem_ld32(taddr + 32, s1);
+  tmem_wait_ld();
+  __half2 h[32];
+  if (kind == 0) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      h[i] = __floats2half2_rn(__uint_as_float(s0[2 * i]), __uint_as_float(s0[2 * i + 1]));
+      h[16 + i] = __floats2half2_rn(__uint_as_float(s1[2 * i]), __uint_as_float(s1[2 * i + 1]));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      h[i] = __floats2half2_rn(i2f_exact(s0[2 * i]) * ss, i2f_exact(s0[2 * i + 1]) * ss);
+      h[16 + i] = __floats2half2_rn(i2f_exact(s1[2 * i]) * ss, i2f_exact(s1[2 * i + 1]) * ss);
+    }
+  }
+  if (lim < kKeys) {
+    const __half ninf = __ushort_as_half(0xFC00);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const __half lo = (2 * i < lim) ? __low2half(h[i]) : ninf;
+      const __half hi = (2 * i + 1 < lim) ? __high2half(h[i]) : ninf;
+      h[i] = __halves2half2(lo, hi);
+    }
+  }
+  __half2 mt[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) mt[i] = __hmax2(h[i], h[16 + i]);
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) mt[i] = __hmax2(mt[i], mt[i + w]);
+  }
+  const float kNegInf = -__int_as_float(0x7f800000);
+  const float mx = fmaxf(__low2float(mt[0]), __high2float(mt[0]));
+  const bool has = mx != kNegInf;
+  o_scale = 1.f;
+  need_rescale = false;
+  if (has && mx > m_used + thr) {
+    const float alpha = ex2_approx(m_used - mx);  // 0 when m_used == -inf
+    need_rescale = (m_used != kNegInf);
+    o_scale = alpha;
+    l *= alpha;
+    m_used = mx;
+  }
+  if (has) {
+    // l accumulates the exponentials before their fp16 rounding (two packed
+    // partial sums); the rounding of p stays exactly the reference's.
+    const uint64_t negm = f32x2_pack(-m_used, -m_used);
+    uint64_t acc0 = 0, acc1 = 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float2 f = __half22float2(h[i]);
+      const float2 d = f32x2_unpack(f32x2_add(f32x2_pack(f.x, f.y), negm));
+      const float e0 = ex2_approx(d.x), e1 = ex2_approx(d.y);
+      const __half2 ph = __floats2half2_rn(e0, e1);
+      if (i & 1)
+        acc1 = f32x2_add(acc1, f32x2_pack(e0, e1));
+      else
+        acc0 = f32x2_add(acc0, f32x2_pack(e0, e1));
+      p[i] = *reinterpret_cast<const uint32_t*>(&ph);
+    }
+    const float2 a0 = f32x2_unpack(acc0), a1 = f32x2_unpack(acc1);
+    l += (a0.x + a0.y) + (a1.x + a1.y);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) p[i] = 0u;
+  }
+}
+
+// Rescale this thread's row of an fp32 O accumulator (D columns) in TMEM.
+template <int D>
+__device__ __forceinline__ void rescale_o_row(uint32_t taddr, float scale) {
+#pragma unroll 1
+  for (int c = 0; c < D; c += 32) {
+    uint32_t o[32];
+    tmem_ld32(taddr + c, o);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * scale);
+    tmem_st32(taddr + c, o);
+  }
+}
+
+// Normalise this thread's O row (D fp32 columns in TMEM) by l and store it as fp16.
+template <int D>
+__device__ __forceinline__ void store_o_row(uint32_t taddr, bool have_o, float l, __half* orow, bool store) {
+#pragma unroll 1
+  for (int c = 0; c < D; c += 32) {
+    uint32_t o[32];
+    if (have_o) {
+      tmem_ld32(taddr + c, o);
+      tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = 0u;
+    }
+    if (store) {
+      // acc / l: reciprocal once per row, then per element one residual
+      // correction (Markstein's method: q0 = a*r, e = a - q0*l, q = q0 + e*r),
+      // which gives the correctly rounded quotient for these normal operands.
+      const float rl = __frcp_rn(l);
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float a0 = __uint_as_float(o[2 * i]), a1 = __uint_as_float(o[2 * i + 1]);
+        const float q0 = a0 * rl, q1 = a1 * rl;
+        w[i] = pack_half2_rn(fmaf(fmaf(-q0, l, a0), rl, q0), fmaf(fmaf(-q1, l, a1), rl, q1));
+      }
+      uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) dst[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+    }
+  }
+}
+
+// Route of 64-key tile j of one map row (mode overrides the bitmask).
+__device__ __forceinline__ int route_kind(int mode, uint64_t bits, int j, int block_n_mask) {
+  if (mode == 1) return 0;  // TM_ROUTE_FP16
+  if (mode == 2) return 1;  // TM_ROUTE_INT8
+  return static_cast<int>((bits >> ((j * kKeys) / block_n_mask)) & 1ull);
+}
+
+// Number of 64-key tiles the reference visits for the query rows
+// [row0, row0 + rows) of a sequence (tilemix.py:603-612), in 64-key units.
+__device__ __forceinline__ int visited_key_tiles(int row0, int rows, int seqlen_q, int seqlen_k, int causal) {
+  int lim = seqlen_k;
+  if (causal) lim = min(seqlen_k, row0 + rows + seqlen_k - seqlen_q);
+  return lim <= 0 ? 0 : (lim + kKeys - 1) / kKeys;
+}
+
+// fp32 value of the fp16 INT8 score scale fp16(f32(fp16(sq * sk)) * qk_scale) (:380-399).
+__device__ __forceinline__ float int8_score_scale(__half sq, __half sk, float qk_scale) {
+  return __half2float(__float2half_rn(__half2float(__hmul(sq, sk)) * qk_scale));
+}
+
+}  // namespace tilemix

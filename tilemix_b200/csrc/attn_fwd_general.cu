@@ -1,0 +1,445 @@
+// Fused FP16/INT8 tile-routed flash-attention forward for B200 (sm_100a).
+//
+// Semantics follow attn_fwd in attention/triton/tilemix.py:503-951:
+//   * program -> (query tile, Q head, sequence); KV head = hq / (HQ/HK) (:585-592)
+//   * per-sequence lengths from cu_seqlens (:594-601), causal tile bound (:603-612)
+//   * q_fp16 = fp16(q * sm_scale*log2e) (:641-649); q8 / per-block Q scale (:651-695)
+//   * each key tile is routed by bit (key_start / block_n_mask) of the row word
+//     pm[hk * m_blocks + start_m] (:818-933): FP16 QK^T (:210-300) or INT8 QK^T
+//     with qk = fp16(f32(i32) * f32(fp16(fp16(sq*sk) * qk_scale))) (:303-404)
+//   * shared online softmax, p = fp16(exp2(f32(qk) - m)) (:179-207); PV with
+//     FP16 P and V, FP32 accumulation (:284-299, :432-448); out = acc / l (:935-951)
+//
+// B200 mapping (one CTA = 128 query rows of one head; TMEM lane r = row r):
+//   warp 4     TMA producer: K (fp16 and/or int8, only the routed formats) and V
+//              tiles of 64 keys into a 3-stage shared-memory ring.
+//   warp 5     MMA issuer (one thread): S = Q K^T as tcgen05.mma with Q as the
+//              TMEM operand (kind::f16 -> fp32 S, or kind::i8 -> int32 S), and
+//              O += P V with P as the TMEM operand (kind::f16, fp32 O in TMEM).
+//   warps 0-3  softmax: load Q once (scaled fp16 and int8 codes, quantised in
+//              kernel when no prequantised Q is given), then per key tile read S
+//              from TMEM, apply the reference rounding chain, write P (fp16) back
+//              into TMEM over S, and finally normalise O and store it.
+// S/P live in three 64-column TMEM slots so that QK^T of tile j+1 and PV of
+// tile j-1 run on the tensor core while the softmax works on tile j.
+//
+// Rescaling of O: with rescale_threshold == 0 the running max is updated on
+// every increase exactly as in the reference. With a positive threshold t
+// (log2 units) the reference max is only moved when the tile max exceeds it by
+// more than t, so P may reach 2^t (fp16-safe for t <= 15) and O is rescaled in
+// TMEM only on those rare jumps; the result is the same softmax up to fp16
+// rounding of P.
+#include "attn_common.cuh"
+#include "tilemix_b200.h"
+
+namespace tilemix {
+namespace general {
+
+constexpr int kRows = 128;
+constexpr int kStages = 3;
+constexpr int kSlots = 3;
+constexpr int kThreads = 192;
+
+// TMEM columns (32-bit) of the 512 allocated per CTA.
+constexpr uint32_t kColO = 0;      // O accumulator, head_dim columns (<=128)
+constexpr uint32_t kColS = 128;    // 3 slots x 64 columns (S fp32/int32, then P fp16 in the first 32)
+constexpr uint32_t kColX = 320;    // second-format S of a split-route tile (block_m == 64 only)
+constexpr uint32_t kColQ16 = 384;  // scaled fp16 Q, head_dim/2 columns
+constexpr uint32_t kColQ8 = 448;   // int8 Q codes, head_dim/4 columns
+constexpr uint32_t kTmemCols = 512;
+
+// Shared memory (offsets from a 1024-byte aligned base).
+constexpr uint32_t kK16Bytes = 64 * 128 * 2;  // one stage of fp16 K (head_dim <= 128)
+constexpr uint32_t kK8Bytes = 64 * 128;       // one stage of int8 K
+constexpr uint32_t kVBytes = 64 * 128 * 2;    // one stage of fp16 V
+constexpr uint32_t kOffK16 = 0;
+constexpr uint32_t kOffV = kOffK16 + kStages * kK16Bytes;
+constexpr uint32_t kOffK8 = kOffV + kStages * kVBytes;
+constexpr uint32_t kOffBar = kOffK8 + kStages * kK8Bytes;
+constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // barriers + alignment slack
+
+
+struct Barriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t s_full[kSlots];
+  uint64_t p_ready[kSlots];
+  uint64_t pv_done[kSlots];
+  uint64_t q_ready;
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  float red[4];
+};
+
+// Per-CTA routing context, identical in every thread.
+struct Route {
+  uint64_t bits[2];  // map row word per 64-row half (or the single 128-row word)
+  int nb[2];         // number of 64-key tiles each half processes
+  int halves;        // 1 (block_m 128) or 2 (block_m 64)
+  int mode;
+  int bnm_shift_div;  // block_n_mask (keys per routing bit)
+
+  __device__ __forceinline__ int kind(int h, int j) const { return route_kind(mode, bits[h], j, bnm_shift_div); }
+  __device__ __forceinline__ void needs(int j, bool& n16, bool& n8) const {
+    n16 = false;
+    n8 = false;
+    for (int h = 0; h < halves; ++h) {
+      if (j < nb[h]) {
+        if (kind(h, j))
+          n8 = true;
+        else
+          n16 = true;
+      }
+    }
+  }
+};
+
+__device__ __forceinline__ void named_bar_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    tilemix_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_k16, const __grid_constant__ CUtensorMap tm_k8,
+                            const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kOffBar);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tile = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
+  const int hq = blockIdx.y;
+  const int b = blockIdx.z;
+
+  const int q_start = a.cu_q[b];
+  const int seqlen_q = a.cu_q[b + 1] - q_start;
+  if (tile * kRows >= seqlen_q) return;  // uniform: before any barrier or allocation
+  const int k_start = a.cu_k[b];
+  const int seqlen_k = a.cu_k[b + 1] - k_start;
+  const int hk = hq / a.group;
+  const int coff = seqlen_k - seqlen_q;
+
+  Route rt;
+  rt.halves = kRows / a.block_m;
+  rt.mode = a.mode;
+  rt.bnm_shift_div = a.block_n_mask;
+  const int m_blocks = (seqlen_q + a.block_m - 1) / a.block_m;
+  int n_tiles = 0;
+  for (int h = 0; h < 2; ++h) {
+    rt.bits[h] = 0;
+    rt.nb[h] = 0;
+    if (h >= rt.halves) continue;
+    const int mrow = tile * rt.halves + h;
+    if (mrow * a.block_m >= seqlen_q) continue;
+    if (a.mode == TM_ROUTE_MIXED) rt.bits[h] = a.bitmask[static_cast<int64_t>(hk) * m_blocks + mrow];
+    int lim = seqlen_k;
+    if (a.causal) lim = min(seqlen_k, (mrow + 1) * a.block_m + coff);
+    rt.nb[h] = lim <= 0 ? 0 : (lim + kKeys - 1) / kKeys;
+    n_tiles = max(n_tiles, rt.nb[h]);
+  }
+
+  const uint32_t k16_box_bytes = 64 * 64 * 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&bars->s_full[s], 1);
+      mbar_init(&bars->p_ready[s], kRows);
+      mbar_init(&bars->pv_done[s], 1);
+    }
+    mbar_init(&bars->q_ready, kRows);
+    mbar_init(&bars->mma_done, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_k16);
+      prefetch_tmap(&tm_v);
+      if (a.mode != TM_ROUTE_FP16) prefetch_tmap(&tm_k8);
+      bool ok = true;
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int s = j % kStages;
+        if (j >= kStages) ok = mbar_wait(&bars->empty[s], ((j - kStages) / kStages) & 1, a.err, kErrTimeoutEmpty);
+        if (!ok) break;
+        bool n16, n8;
+        rt.needs(j, n16, n8);
+        const uint32_t vbytes = static_cast<uint32_t>(D) * 64 * 2;
+        const uint32_t bytes = vbytes + (n16 ? vbytes : 0u) + (n8 ? static_cast<uint32_t>(D) * 64 : 0u);
+        mbar_arrive_expect_tx(&bars->full[s], bytes);
+        const int tok = k_start + j * kKeys;
+#pragma unroll
+        for (int box = 0; box < D / 64; ++box) {
+          if (n16) tma_load_3d(smem + kOffK16 + s * kK16Bytes + box * k16_box_bytes, &tm_k16, &bars->full[s], box * 64, hk, tok);
+          tma_load_3d(smem + kOffV + s * kVBytes + box * k16_box_bytes, &tm_v, &bars->full[s], box * 64, hk, tok);
+        }
+        if (n8) tma_load_3d(smem + kOffK8 + s * kK8Bytes, &tm_k8, &bars->full[s], 0, hk, tok);
+      }
+      // Drain: every issued copy must land before the CTA exits.
+      const int first = max(0, n_tiles - kStages);
+      for (int j = first; j < n_tiles; ++j) {
+        mbar_wait(&bars->full[j % kStages], (j / kStages) & 1, a.err, kErrTimeoutDrain);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk16 = make_idesc(1, 0, 0, 0, 128, 64);
+      const uint32_t idesc_qk8 = make_idesc(2, 1, 0, 0, 128, 64);
+      const uint32_t idesc_pv = make_idesc(1, 0, 0, 1, 128, static_cast<uint32_t>(D));
+      const uint32_t k8_layout = (D == 128) ? 2u : 4u;
+      const uint32_t k8_sbo = (D == 128) ? 1024u : 512u;
+      bool ok = mbar_wait(&bars->q_ready, 0, a.err, kErrTimeoutQ);
+      tc_fence_after();
+      bool prev_split = false;
+      for (int j = 0; ok && j <= n_tiles; ++j) {
+        if (j < n_tiles) {
+          const int s = j % kStages;
+          const int slot = j % kSlots;
+          ok = mbar_wait(&bars->full[s], (j / kStages) & 1, a.err, kErrTimeoutFull);
+          if (ok && j >= kSlots) ok = mbar_wait(&bars->pv_done[slot], ((j - kSlots) / kSlots) & 1, a.err, kErrTimeoutPV);
+          bool n16, n8;
+          rt.needs(j, n16, n8);
+          const bool split = n16 && n8;
+          if (ok && split && prev_split)
+            ok = mbar_wait(&bars->p_ready[(j - 1) % kSlots], ((j - 1) / kSlots) & 1, a.err, kErrTimeoutP);
+          if (!ok) break;
+          prev_split = split;
+          tc_fence_after();
+          const uint32_t s_col = kColS + slot * 64;
+          if (n16) {
+            const uint32_t kbase = smem_u32(smem + kOffK16 + s * kK16Bytes);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint64_t bdesc = make_sdesc(kbase + (kk >> 2) * k16_box_bytes + (kk & 3) * 32, 16, 1024, 2);
+              mma_f16_ts(tbase + s_col, tbase + kColQ16 + kk * 8, bdesc, idesc_qk16, kk > 0 ? 1u : 0u);
+            }
+          }
+          if (n8) {
+            const uint32_t dcol = split ? kColX : s_col;
+            const uint32_t kbase = smem_u32(smem + kOffK8 + s * kK8Bytes);
+            for (int kk = 0; kk < D / 32; ++kk) {
+              const uint64_t bdesc = make_sdesc(kbase + kk * 32, 16, k8_sbo, k8_layout);
+              mma_i8_ts(tbase + dcol, tbase + kColQ8 + kk * 8, bdesc, idesc_qk8, kk > 0 ? 1u : 0u);
+            }
+          }
+          tc_commit(&bars->s_full[slot]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1;
+          const int s = jj % kStages;
+          const int slot = jj % kSlots;
+          ok = mbar_wait(&bars->p_ready[slot], (jj / kSlots) & 1, a.err, kErrTimeoutP);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t vbase = smem_u32(smem + kOffV + s * kVBytes);
+          const uint32_t p_col = kColS + slot * 64;
+          for (int kk = 0; kk < kKeys / 16; ++kk) {
+            const uint64_t bdesc = make_sdesc(vbase + kk * 16 * 128, k16_box_bytes, 1024, 2);
+            mma_f16_ts(tbase + kColO, tbase + p_col + kk * 8, bdesc, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&bars->pv_done[slot]);
+          tc_commit(&bars->empty[s]);
+        }
+      }
+      // All issued tensor-core work must finish before TMEM is released.
+      tc_commit(&bars->mma_done);
+      mbar_wait(&bars->mma_done, 0, a.err, kErrTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax warps 0-3
+    const int t = threadIdx.x;  // row within the CTA tile == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int row = tile * kRows + t;
+    const bool row_ok = row < seqlen_q;
+    const int half = t / a.block_m;  // 0 for block_m 128
+
+    // ---- Q: scaled fp16 codes and int8 codes into TMEM
+    const __half* qrow = a.q + (static_cast<int64_t>(q_start) + row) * a.q_st + static_cast<int64_t>(hq) * a.q_sh;
+    __half sq16 = __float2half_rn(1.f);
+    {
+      uint4 raw[D / 8];
+#pragma unroll
+      for (int c8 = 0; c8 < D / 8; ++c8) raw[c8] = row_ok ? __ldg(reinterpret_cast<const uint4*>(qrow + c8 * 8))
+                                                        : make_uint4(0, 0, 0, 0);
+      uint32_t packed[D / 2];
+      float amax = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < D / 8; ++c8) {
+        const __half2* h = reinterpret_cast<const __half2*>(&raw[c8]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(h[e]);
+          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+          packed[c8 * 4 + e] = pack_half2_rn(f.x * a.qk_scale, f.y * a.qk_scale);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < D / 2; c += 16) tmem_st16(tbase + lane_off + kColQ16 + c, packed + c);
+      if (a.mode != TM_ROUTE_FP16) {
+        uint32_t codes[D / 4];
+        if (a.fuse_q) {
+          // Block absmax over the 128 rows of this head = one BLKQ=128 quantisation block.
+          float m = amax;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0) bars->red[warp] = m;
+          named_bar_sync_softmax();
+          m = fmaxf(fmaxf(bars->red[0], bars->red[1]), fmaxf(bars->red[2], bars->red[3]));
+          const float scale = __fdiv_rn(m, 127.f);
+          sq16 = __float2half_rn(scale);
+#pragma unroll
+          for (int c8 = 0; c8 < D / 8; ++c8) {
+            const __half2* h = reinterpret_cast<const __half2*>(&raw[c8]);
+            uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(h[e]);
+              const uint32_t pr = (static_cast<uint32_t>(quant_code(f.x, scale)) & 0xFFu) |
+                                  ((static_cast<uint32_t>(quant_code(f.y, scale)) & 0xFFu) << 8);
+              if (e < 2)
+                w0 |= pr << (16 * e);
+              else
+                w1 |= pr << (16 * (e - 2));
+            }
+            codes[c8 * 2] = w0;
+            codes[c8 * 2 + 1] = w1;
+          }
+        } else {
+          const int8_t* q8row =
+              a.q8 + (static_cast<int64_t>(q_start) + row) * a.q8_st + static_cast<int64_t>(hq) * a.q8_sh;
+#pragma unroll
+          for (int c16 = 0; c16 < D / 16; ++c16) {
+            uint4 u = make_uint4(0, 0, 0, 0);
+            if (row_ok) u = __ldg(reinterpret_cast<const uint4*>(q8row + c16 * 16));
+            codes[c16 * 4 + 0] = u.x;
+            codes[c16 * 4 + 1] = u.y;
+            codes[c16 * 4 + 2] = u.z;
+            codes[c16 * 4 + 3] = u.w;
+          }
+          const int qs_base = a.cu_qs[b];
+          const int qs_end = a.cu_qs[b + 1];
+          if (qs_end > qs_base && row_ok) {
+            const int idx = min(qs_base + row / a.blkq, qs_end - 1);
+            sq16 = a.q_scale[static_cast<int64_t>(idx) * a.HQ + hq];
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < D / 4; c += 16) tmem_st16(tbase + lane_off + kColQ8 + c, codes + c);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars->q_ready);
+    }
+
+    const int ks_base = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[b] : 0;
+    const int ks_end = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[b + 1] : 0;
+    const float kNegInf = -__int_as_float(0x7f800000);
+    float m_used = kNegInf;
+    float l = 1.f;
+    const int my_nb = rt.nb[half];
+    bool ok = true;
+
+    for (int j = 0; j < n_tiles; ++j) {
+      const int slot = j % kSlots;
+      const bool active = j < my_nb;  // uniform per warp (a warp never straddles halves)
+      const int kind = active ? rt.kind(half, j) : 0;
+      bool n16, n8;
+      rt.needs(j, n16, n8);
+      const uint32_t src_col = (kind == 1 && n16 && n8) ? kColX : (kColS + slot * 64);
+      float ss = 1.f;
+      if (active && kind == 1) {
+        __half sk16 = __float2half_rn(1.f);
+        if (ks_end > ks_base) {
+          const int idx = min(ks_base + (j * kKeys) / a.blkk, ks_end - 1);
+          sk16 = a.k_scale[static_cast<int64_t>(idx) * a.HK + hk];
+        }
+        ss = int8_score_scale(sq16, sk16, a.qk_scale);
+      }
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[slot], (j / kSlots) & 1, a.err, kErrTimeoutScores));
+      if (!ok) break;
+      tc_fence_after();
+
+      uint32_t p[32];
+      float o_scale = 1.f;
+      bool need_rescale = false;
+      if (active) {
+        int lim = seqlen_k - j * kKeys;
+        if (a.causal) lim = min(lim, row + coff + 1 - j * kKeys);
+        softmax_tile(tbase + lane_off + src_col, kind, ss, lim, a.rescale_threshold, m_used, l, p, o_scale,
+                     need_rescale);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p[i] = 0u;
+      }
+
+      if (__any_sync(0xffffffffu, need_rescale)) {
+        // O must hold PV(j-1) before it is rescaled; PV(j) waits for our P.
+        const int jj = j - 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[jj % kSlots], (jj / kSlots) & 1, a.err, kErrTimeoutPV));
+        if (!ok) break;
+        tc_fence_after();
+        rescale_o_row<D>(tbase + lane_off + kColO, o_scale);
+      }
+      tmem_st32(tbase + lane_off + kColS + slot * 64, p);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars->p_ready[slot]);
+    }
+
+    // ---- epilogue: O / l -> fp16
+    __half* orow = a.out + (static_cast<int64_t>(q_start) + row) * a.o_st + static_cast<int64_t>(hq) * a.o_sh;
+    if (n_tiles > 0 && ok) {
+      const int jj = n_tiles - 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[jj % kSlots], (jj / kSlots) & 1, a.err, kErrTimeoutPV));
+      tc_fence_after();
+    }
+    store_o_row<D>(tbase + lane_off + kColO, n_tiles > 0, l, orow, row_ok && ok);
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+
+}  // namespace general
+
+// Launch the general kernel (any supported block_m, head_dim 64/128, prequantised or fused Q).
+int launch_attn_general(const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v, const AttnArgs& a,
+                        int tiles, int heads_q, int batch, cudaStream_t stream) {
+  using namespace general;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TM_ERR_LAUNCH;
+  static bool attr_set[64] = {};
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(tilemix_attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(tilemix_attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess)
+      return TM_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  dim3 grid(tiles, heads_q, batch);
+  if (a.D == 128)
+    tilemix_attn_fwd_kernel<128><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, a);
+  else
+    tilemix_attn_fwd_kernel<64><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, a);
+  return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
+}
+
+}  // namespace tilemix

@@ -1,0 +1,454 @@
+// Paired-tile TileMix attention forward for B200 (sm_100a): the fast path for
+// head_dim 128, block_m 128 and in-kernel Q quantisation (BLKQ = 128), which is
+// what the model integration and tilemix_attention_with_quant use.
+//
+// Same semantics as the general kernel (attention/triton/tilemix.py:503-951);
+// different mapping. One CTA owns two 128-row query tiles X = A, B that share a
+// KV head: either two Q heads of one GQA group at the same query block (their
+// routing words are the same map row), or two consecutive query blocks of one
+// head. Every K/V tile is loaded once into shared memory and feeds both tiles.
+//
+//   warps 0-3 / 4-7   softmax warpgroup of tile A / B (thread = query row =
+//                     TMEM lane). At start: scale Q in place in shared memory
+//                     (fp16(q * sm_scale * log2e)) and quantise it per 128-row
+//                     block into the INT8 operand (BLKQ = 128 block = the tile).
+//   warp 8            TMA producer: Q tiles, then K (only the formats routed by
+//                     either tile) and V tiles of 64 keys, 3-stage ring.
+//   warp 9            MMA issuer: S_X = Q_X K^T (tcgen05 kind::f16 or kind::i8,
+//                     both operands in shared memory) into a TMEM score slot of
+//                     tile X; O_X += P_X V (kind::f16, P from TMEM, fp32 O).
+// TMEM (512 columns): O_A [0,128), O_B [128,256), two 64-column S/P slots per
+// tile at [256,384) and [384,512). Issue order per key tile j:
+//   S_A(j), S_B(j), PV_A(j-1), PV_B(j-1)
+// so that every wait of the MMA thread has other tensor-core work queued.
+#include "attn_common.cuh"
+#include "tilemix_b200.h"
+
+namespace tilemix {
+namespace paired {
+
+constexpr int kD = 128;
+constexpr int kRows = 128;
+constexpr int kStages = 3;
+constexpr int kPrefetch = 8;  // key tiles warmed in L2 ahead of the TMA ring
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+
+constexpr uint32_t kQ16Bytes = kRows * kD * 2;  // 32 KB, two 64-column boxes of 16 KB
+constexpr uint32_t kQ8Bytes = kRows * kD;       // 16 KB
+constexpr uint32_t kK16Bytes = kKeys * kD * 2;  // 16 KB
+constexpr uint32_t kK8Bytes = kKeys * kD;       // 8 KB
+constexpr uint32_t kVBytes = kKeys * kD * 2;    // 16 KB
+constexpr uint32_t kOffQ16 = 0;
+constexpr uint32_t kOffQ8 = kOffQ16 + 2 * kQ16Bytes;
+constexpr uint32_t kOffK16 = kOffQ8 + 2 * kQ8Bytes;
+constexpr uint32_t kOffV = kOffK16 + kStages * kK16Bytes;
+constexpr uint32_t kOffK8 = kOffV + kStages * kVBytes;
+constexpr uint32_t kOffBar = kOffK8 + kStages * kK8Bytes;
+constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+
+struct Barriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t q_full[2];
+  uint64_t q_ready[2];
+  uint64_t s_full[2][2];
+  uint64_t p_ready[2][2];
+  uint64_t pv_done[2][2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  float red[2][4];
+};
+
+struct QTile {
+  uint64_t bits;
+  int hq;
+  int mtile;
+  int nb;  // 64-key tiles visited (0 = tile absent)
+};
+
+__device__ __forceinline__ uint32_t col_o(int x) { return static_cast<uint32_t>(x) * 128u; }
+__device__ __forceinline__ uint32_t col_s(int x, int slot) {
+  return 256u + static_cast<uint32_t>(x) * 128u + static_cast<uint32_t>(slot) * 64u;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    tilemix_attn_fwd_paired_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k16,
+                                   const __grid_constant__ CUtensorMap tm_k8, const __grid_constant__ CUtensorMap tm_v,
+                                   const AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kOffBar);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.z;
+  const int q_start = a.cu_q[b];
+  const int seqlen_q = a.cu_q[b + 1] - q_start;
+  const int k_start = a.cu_k[b];
+  const int seqlen_k = a.cu_k[b + 1] - k_start;
+  const int m_blocks = (seqlen_q + kRows - 1) / kRows;
+
+  QTile tl[2];
+  const int rev = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    if (a.pair_heads) {
+      tl[x].hq = 2 * static_cast<int>(blockIdx.y) + x;
+      tl[x].mtile = rev;
+    } else {
+      tl[x].hq = blockIdx.y;
+      tl[x].mtile = 2 * rev + x;
+    }
+    const bool valid = tl[x].mtile * kRows < seqlen_q;
+    tl[x].nb = valid ? visited_key_tiles(tl[x].mtile * kRows, kRows, seqlen_q, seqlen_k, a.causal) : 0;
+    tl[x].bits = 0;
+    if (valid && a.mode == TM_ROUTE_MIXED)
+      tl[x].bits = a.bitmask[static_cast<int64_t>(tl[x].hq / a.group) * m_blocks + tl[x].mtile];
+  }
+  const bool valid0 = tl[0].mtile * kRows < seqlen_q;
+  const bool valid1 = tl[1].mtile * kRows < seqlen_q;
+  if (!valid0 && !valid1) return;  // uniform, before any barrier or allocation
+  const int hk = tl[0].hq / a.group;  // both tiles share the KV head
+  const int n_iter = max(tl[0].nb, tl[1].nb);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars->q_full[x], 1);
+      mbar_init(&bars->q_ready[x], kRows);
+      for (int s = 0; s < 2; ++s) {
+        mbar_init(&bars->s_full[x][s], 1);
+        mbar_init(&bars->p_ready[x][s], kRows);
+        mbar_init(&bars->pv_done[x][s], 1);
+      }
+    }
+    mbar_init(&bars->mma_done, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_k16);
+      prefetch_tmap(&tm_v);
+      if (a.mode != TM_ROUTE_FP16) prefetch_tmap(&tm_k8);
+      for (int x = 0; x < 2; ++x) {
+        if (tl[x].mtile * kRows >= seqlen_q) continue;
+        mbar_arrive_expect_tx(&bars->q_full[x], kQ16Bytes);
+        for (int box = 0; box < 2; ++box)
+          tma_load_3d(smem + kOffQ16 + x * kQ16Bytes + box * (kQ16Bytes / 2), &tm_q, &bars->q_full[x], box * 64,
+                      tl[x].hq, q_start + tl[x].mtile * kRows);
+      }
+      bool ok = true;
+      for (int j = 0; j < n_iter && ok; ++j) {
+        const int s = j % kStages;
+        if (j >= kStages) ok = mbar_wait(&bars->empty[s], ((j - kStages) / kStages) & 1, a.err, kErrTimeoutEmpty);
+        if (!ok) break;
+        bool n16 = false, n8 = false;
+        for (int x = 0; x < 2; ++x) {
+          if (j < tl[x].nb) {
+            if (route_kind(a.mode, tl[x].bits, j, a.block_n_mask))
+              n8 = true;
+            else
+              n16 = true;
+          }
+        }
+        const uint32_t bytes = kVBytes + (n16 ? kK16Bytes : 0u) + (n8 ? kK8Bytes : 0u);
+        mbar_arrive_expect_tx(&bars->full[s], bytes);
+        const int tok = k_start + j * kKeys;
+        for (int box = 0; box < 2; ++box) {
+          if (n16)
+            tma_load_3d(smem + kOffK16 + s * kK16Bytes + box * (kK16Bytes / 2), &tm_k16, &bars->full[s], box * 64,
+                        hk, tok);
+          tma_load_3d(smem + kOffV + s * kVBytes + box * (kVBytes / 2), &tm_v, &bars->full[s], box * 64, hk, tok);
+        }
+        if (n8) tma_load_3d(smem + kOffK8 + s * kK8Bytes, &tm_k8, &bars->full[s], 0, hk, tok);
+        // Every CTA of this KV head walks the keys at the same pace, so a tile
+        // that misses L2 misses for all of them: warm L2 kPrefetch tiles ahead.
+        const int jp = (j == 0) ? 1 : j + kPrefetch;
+        for (int jq = jp; jq <= j + kPrefetch && jq < n_iter; ++jq) {
+          bool p16 = false, p8 = false;
+          for (int x = 0; x < 2; ++x) {
+            if (jq < tl[x].nb) {
+              if (route_kind(a.mode, tl[x].bits, jq, a.block_n_mask))
+                p8 = true;
+              else
+                p16 = true;
+            }
+          }
+          const int ptok = k_start + jq * kKeys;
+          for (int box = 0; box < 2; ++box) {
+            if (p16) tma_prefetch_l2_3d(&tm_k16, box * 64, hk, ptok);
+            tma_prefetch_l2_3d(&tm_v, box * 64, hk, ptok);
+          }
+          if (p8) tma_prefetch_l2_3d(&tm_k8, 0, hk, ptok);
+        }
+      }
+      const int first = max(0, n_iter - kStages);
+      for (int j = first; j < n_iter; ++j)
+        mbar_wait(&bars->full[j % kStages], (j / kStages) & 1, a.err, kErrTimeoutDrain);
+      for (int x = 0; x < 2; ++x)
+        if (tl[x].mtile * kRows < seqlen_q) mbar_wait(&bars->q_full[x], 0, a.err, kErrTimeoutDrain);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA issuer
+    // Event loop: each tile X is an independent stream of S(j) and PV(j)
+    // launches; whichever launch has its inputs ready is issued, so neither
+    // tile nor the TMA ring blocks the other's work.
+    if (lane == 0) {
+      const uint32_t idesc_qk16 = make_idesc(1, 0, 0, 0, 128, 64);
+      const uint32_t idesc_qk8 = make_idesc(2, 1, 0, 0, 128, 64);
+      const uint32_t idesc_pv = make_idesc(1, 0, 0, 1, 128, kD);
+      bool ok = true;
+      for (int x = 0; x < 2 && ok; ++x)
+        if (tl[x].mtile * kRows < seqlen_q) ok = mbar_wait(&bars->q_ready[x], 0, a.err, kErrTimeoutQ);
+      tc_fence_after();
+      int s_next[2] = {0, 0};
+      int pv_next[2] = {0, 0};
+      int released = 0;
+      unsigned long long t_last = globaltimer_ns();
+      while (ok) {
+        bool progress = false;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const int nb = tl[x].nb;
+          // PV_X(jj) once P_X(jj) is in TMEM.
+          if (pv_next[x] < s_next[x]) {
+            const int jj = pv_next[x];
+            const int slot = jj & 1;
+            if (mbar_test(&bars->p_ready[x][slot], (jj >> 1) & 1)) {
+              tc_fence_after();
+              const uint32_t vb = smem_u32(smem + kOffV + (jj % kStages) * kVBytes);
+#pragma unroll
+              for (int kk = 0; kk < kKeys / 16; ++kk) {
+                const uint64_t bd = make_sdesc(vb + kk * 16 * 128, kVBytes / 2, 1024, 2);
+                mma_f16_ts(tbase + col_o(x), tbase + col_s(x, slot) + kk * 8, bd, idesc_pv,
+                           (jj > 0 || kk > 0) ? 1u : 0u);
+              }
+              tc_commit(&bars->pv_done[x][slot]);
+              ++pv_next[x];
+              progress = true;
+            }
+          }
+          // S_X(j) once K(j) is resident and slot j&1 is free (PV_X(j-2) done).
+          if (s_next[x] < nb) {
+            const int j = s_next[x];
+            const int s = j % kStages;
+            const int slot = j & 1;
+            if (mbar_test(&bars->full[s], (j / kStages) & 1) &&
+                (j < 2 || mbar_test(&bars->pv_done[x][slot], ((j - 2) >> 1) & 1))) {
+              tc_fence_after();
+              const uint32_t d = tbase + col_s(x, slot);
+              if (route_kind(a.mode, tl[x].bits, j, a.block_n_mask) == 0) {
+                const uint32_t qb = smem_u32(smem + kOffQ16 + x * kQ16Bytes);
+                const uint32_t kb = smem_u32(smem + kOffK16 + s * kK16Bytes);
+#pragma unroll
+                for (int kk = 0; kk < kD / 16; ++kk) {
+                  const uint64_t ad = make_sdesc(qb + (kk >> 2) * (kQ16Bytes / 2) + (kk & 3) * 32, 16, 1024, 2);
+                  const uint64_t bd = make_sdesc(kb + (kk >> 2) * (kK16Bytes / 2) + (kk & 3) * 32, 16, 1024, 2);
+                  mma_f16_ss(d, ad, bd, idesc_qk16, kk > 0 ? 1u : 0u);
+                }
+              } else {
+                const uint32_t qb = smem_u32(smem + kOffQ8 + x * kQ8Bytes);
+                const uint32_t kb = smem_u32(smem + kOffK8 + s * kK8Bytes);
+#pragma unroll
+                for (int kk = 0; kk < kD / 32; ++kk) {
+                  const uint64_t ad = make_sdesc(qb + kk * 32, 16, 1024, 2);
+                  const uint64_t bd = make_sdesc(kb + kk * 32, 16, 1024, 2);
+                  mma_i8_ss(d, ad, bd, idesc_qk8, kk > 0 ? 1u : 0u);
+                }
+              }
+              tc_commit(&bars->s_full[x][slot]);
+              ++s_next[x];
+              progress = true;
+            }
+          }
+        }
+        // Release a K/V stage once every tile that uses it has issued its PV.
+        while (released < n_iter && (pv_next[0] > released || tl[0].nb <= released) &&
+               (pv_next[1] > released || tl[1].nb <= released)) {
+          tc_commit(&bars->empty[released % kStages]);
+          ++released;
+          progress = true;
+        }
+        if (pv_next[0] >= tl[0].nb && pv_next[1] >= tl[1].nb && released >= n_iter) break;
+        const unsigned long long now = globaltimer_ns();
+        if (progress) {
+          t_last = now;
+        } else if (now - t_last > kWaitTimeoutNs) {
+          record_error(a.err, kErrTimeoutP);
+          ok = false;
+        }
+      }
+      tc_commit(&bars->mma_done);
+      mbar_wait(&bars->mma_done, 0, a.err, kErrTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax warpgroups
+    const int x = warp >> 2;
+    const int t = threadIdx.x & 127;  // row within the tile == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const QTile me = tl[x];
+    const bool tile_ok = me.mtile * kRows < seqlen_q;
+    if (tile_ok) {
+      const int row = me.mtile * kRows + t;
+      const bool row_ok = row < seqlen_q;
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->q_full[x], 0, a.err, kErrTimeoutQ));
+      __half sq16 = __float2half_rn(1.f);
+      {
+        // Scale Q in place (elementwise, so the swizzled layout is irrelevant)
+        // and build the INT8 operand of this 128-row block.
+        uint8_t* q16 = smem + kOffQ16 + x * kQ16Bytes;
+        uint4 raw[16];
+        float amax = 0.f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          uint4* ptr = reinterpret_cast<uint4*>(q16 + (c >> 3) * (kQ16Bytes / 2) + t * 128 + (((c & 7) ^ (t & 7)) << 4));
+          raw[c] = *ptr;
+          const __half2* h = reinterpret_cast<const __half2*>(&raw[c]);
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(h[e]);
+            if (row_ok) amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+            w[e] = pack_half2_rn(f.x * a.qk_scale, f.y * a.qk_scale);
+          }
+          *ptr = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        if (a.mode != TM_ROUTE_FP16) {
+          float m = amax;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0) bars->red[x][warp & 3] = m;
+          asm volatile("bar.sync %0, 128;" ::"r"(1 + x) : "memory");
+          m = fmaxf(fmaxf(bars->red[x][0], bars->red[x][1]), fmaxf(bars->red[x][2], bars->red[x][3]));
+          const float scale = __fdiv_rn(m, 127.f);
+          sq16 = __float2half_rn(scale);
+          uint8_t* q8 = smem + kOffQ8 + x * kQ8Bytes;
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            // 16 codes of dims [16g, 16g+16) = raw chunks 2g and 2g+1
+            uint32_t w[4];
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc) {
+              const __half2* h = reinterpret_cast<const __half2*>(&raw[2 * g + hc]);
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const float2 f0 = __half22float2(h[2 * e]);
+                const float2 f1 = __half22float2(h[2 * e + 1]);
+                w[hc * 2 + e] = (static_cast<uint32_t>(quant_code(f0.x, scale)) & 0xFFu) |
+                                ((static_cast<uint32_t>(quant_code(f0.y, scale)) & 0xFFu) << 8) |
+                                ((static_cast<uint32_t>(quant_code(f1.x, scale)) & 0xFFu) << 16) |
+                                ((static_cast<uint32_t>(quant_code(f1.y, scale)) & 0xFFu) << 24);
+              }
+            }
+            *reinterpret_cast<uint4*>(q8 + t * 128 + ((g ^ (t & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bars->q_ready[x]);
+      }
+
+      const int ks_base = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[b] : 0;
+      const int ks_end = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[b + 1] : 0;
+      const float kNegInf = -__int_as_float(0x7f800000);
+      float m_used = kNegInf;
+      float l = 1.f;
+      const int coff = seqlen_k - seqlen_q;
+      // K block scale of tile j, loaded one tile ahead to keep the global load
+      // off the critical path.
+      auto load_sk = [&](int j) -> __half {
+        __half v = __float2half_rn(1.f);
+        if (j < me.nb && ks_end > ks_base && route_kind(a.mode, me.bits, j, a.block_n_mask) == 1) {
+          const int idx = min(ks_base + (j * kKeys) / a.blkk, ks_end - 1);
+          v = a.k_scale[static_cast<int64_t>(idx) * a.HK + hk];
+        }
+        return v;
+      };
+      __half sk_next = load_sk(0);
+      for (int j = 0; ok && j < me.nb; ++j) {
+        const int slot = j & 1;
+        const int kind = route_kind(a.mode, me.bits, j, a.block_n_mask);
+        const __half sk16 = sk_next;
+        sk_next = load_sk(j + 1);
+        const float ss = kind == 1 ? int8_score_scale(sq16, sk16, a.qk_scale) : 1.f;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[x][slot], (j >> 1) & 1, a.err, kErrTimeoutScores));
+        if (!ok) break;
+        tc_fence_after();
+        int lim = seqlen_k - j * kKeys;
+        if (a.causal) lim = min(lim, row + coff + 1 - j * kKeys);
+        uint32_t p[32];
+        float o_scale;
+        bool need_rescale;
+        softmax_tile(tbase + lane_off + col_s(x, slot), kind, ss, lim, a.rescale_threshold, m_used, l, p, o_scale,
+                     need_rescale);
+        if (__any_sync(0xffffffffu, need_rescale)) {
+          const int jj = j - 1;
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&bars->pv_done[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutPV));
+          if (!ok) break;
+          tc_fence_after();
+          rescale_o_row<kD>(tbase + lane_off + col_o(x), o_scale);
+        }
+        tmem_st32(tbase + lane_off + col_s(x, slot), p);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars->p_ready[x][slot]);
+      }
+      __half* orow = a.out + (static_cast<int64_t>(q_start) + row) * a.o_st + static_cast<int64_t>(me.hq) * a.o_sh;
+      if (ok && me.nb > 0) {
+        const int jj = me.nb - 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutPV));
+        tc_fence_after();
+      }
+      store_o_row<kD>(tbase + lane_off + col_o(x), me.nb > 0, l, orow, row_ok && ok);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+}  // namespace paired
+
+int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
+                       const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream) {
+  using namespace paired;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TM_ERR_LAUNCH;
+  static bool attr_set[64] = {};
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess)
+      return TM_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  const int mtiles = (max_seqlen_q + kRows - 1) / kRows;
+  dim3 grid;
+  if (a.pair_heads)
+    grid = dim3(mtiles, a.HQ / 2, batch);
+  else
+    grid = dim3((mtiles + 1) / 2, a.HQ, batch);
+  tilemix_attn_fwd_paired_kernel<<<grid, kThreads, kSmemBytes, stream>>>(q, k16, k8, v, a);
+  return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
+}
+
+}  // namespace tilemix

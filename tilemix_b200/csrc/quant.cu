@@ -1,0 +1,149 @@
+// Per-block symmetric INT8 quantiser over varlen packed [tokens, heads, dim]
+// fp16 tensors.
+//
+// Follows attention/triton/quant_per_block_varlen.py:6-45 (kernel) and
+// :48-75 (per_block_int8_single launch): one block = BLK consecutive tokens of
+// one sequence and one head; scale = max|x * sm_scale| / 127 (fp32), code =
+// trunc(x / scale + 0.5 * sign). Scales are laid out [sum_b ceil(T_b/BLK), H]
+// with the per-sequence block offsets in cu_seqlens_scale.
+//
+// B200 design: HBM-bound. One 128-thread CTA per (block, head); every thread
+// keeps its slice of the block in registers between the max pass and the
+// quantise pass, so the input is read from HBM exactly once; 16-byte vector
+// loads, 8-byte vector stores. The grid is (blocks, heads, batch) like the
+// reference's, which gives tens of thousands of CTAs at the BASELINE shapes,
+// far more than the 148 SMs x resident CTAs.
+#include "common.cuh"
+#include "tilemix_b200.h"
+
+namespace tilemix {
+
+constexpr int kQuantThreads = 128;
+constexpr int kQuantMaxVec = 16;  // 16-byte vectors held per thread (BLK*D <= 128*8*16)
+
+__device__ __forceinline__ float block_absmax_reduce(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int w = 1; w < kQuantThreads / 32; ++w) m = fmaxf(m, red[w]);
+  return m;
+}
+
+__global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_kernel(
+    const __half* __restrict__ x, int64_t x_stride_tok, int64_t x_stride_head, const int32_t* __restrict__ cu_seqlens,
+    const int32_t* __restrict__ cu_scale, int heads, int dim, int blk, float sm_scale, int8_t* __restrict__ out,
+    int64_t o_stride_tok, int64_t o_stride_head, float* __restrict__ scale_f32, __half* __restrict__ scale_f16) {
+  __shared__ float red[kQuantThreads / 32];
+  const int off_blk = blockIdx.x, off_h = blockIdx.y, off_b = blockIdx.z;
+  const int start = cu_seqlens[off_b];
+  const int len = cu_seqlens[off_b + 1] - start;
+  if (off_blk * blk >= len) return;
+  const int rows = min(blk, len - off_blk * blk);
+  const int vec_per_row = dim >> 3;
+  const int nvec = rows * vec_per_row;
+  const int64_t tok0 = static_cast<int64_t>(start) + static_cast<int64_t>(off_blk) * blk;
+  const __half* xb = x + tok0 * x_stride_tok + static_cast<int64_t>(off_h) * x_stride_head;
+  int8_t* ob = out + tok0 * o_stride_tok + static_cast<int64_t>(off_h) * o_stride_head;
+
+  float amax = 0.f;
+  const bool in_regs = (blk * vec_per_row) <= kQuantThreads * kQuantMaxVec;
+  uint4 regs[kQuantMaxVec];
+  if (in_regs) {
+#pragma unroll
+    for (int i = 0; i < kQuantMaxVec; ++i) {
+      const int v = i * kQuantThreads + threadIdx.x;
+      regs[i] = make_uint4(0, 0, 0, 0);
+      if (v < nvec) {
+        const int r = v / vec_per_row, c = (v % vec_per_row) << 3;
+        regs[i] = __ldg(reinterpret_cast<const uint4*>(xb + r * x_stride_tok + c));
+        const __half2* h = reinterpret_cast<const __half2*>(&regs[i]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float2 f = __half22float2(h[e]);
+          amax = fmaxf(amax, fmaxf(fabsf(f.x * sm_scale), fabsf(f.y * sm_scale)));
+        }
+      }
+    }
+  } else {
+    for (int v = threadIdx.x; v < nvec; v += kQuantThreads) {
+      const int r = v / vec_per_row, c = (v % vec_per_row) << 3;
+      uint4 u = __ldg(reinterpret_cast<const uint4*>(xb + r * x_stride_tok + c));
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __half22float2(h[e]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x * sm_scale), fabsf(f.y * sm_scale)));
+      }
+    }
+  }
+  amax = block_absmax_reduce(amax, red);
+  const float scale = __fdiv_rn(amax, 127.f);
+
+  auto quant_vec = [&](const uint4& u) -> uint2 {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __half22float2(h[e]);
+      const uint32_t a = static_cast<uint32_t>(quant_code(f.x * sm_scale, scale)) & 0xFFu;
+      const uint32_t b = static_cast<uint32_t>(quant_code(f.y * sm_scale, scale)) & 0xFFu;
+      const uint32_t pair = a | (b << 8);
+      if (e < 2)
+        lo |= pair << (16 * e);
+      else
+        hi |= pair << (16 * (e - 2));
+    }
+    return make_uint2(lo, hi);
+  };
+
+  if (in_regs) {
+#pragma unroll
+    for (int i = 0; i < kQuantMaxVec; ++i) {
+      const int v = i * kQuantThreads + threadIdx.x;
+      if (v < nvec) {
+        const int r = v / vec_per_row, c = (v % vec_per_row) << 3;
+        *reinterpret_cast<uint2*>(ob + r * o_stride_tok + c) = quant_vec(regs[i]);
+      }
+    }
+  } else {
+    for (int v = threadIdx.x; v < nvec; v += kQuantThreads) {
+      const int r = v / vec_per_row, c = (v % vec_per_row) << 3;
+      uint4 u = __ldg(reinterpret_cast<const uint4*>(xb + r * x_stride_tok + c));
+      *reinterpret_cast<uint2*>(ob + r * o_stride_tok + c) = quant_vec(u);
+    }
+  }
+  if (threadIdx.x == 0) {
+    const int64_t sidx = (static_cast<int64_t>(cu_scale[off_b]) + off_blk) * heads + off_h;
+    if (scale_f32 != nullptr) scale_f32[sidx] = scale;
+    if (scale_f16 != nullptr) scale_f16[sidx] = __float2half_rn(scale);
+  }
+}
+
+}  // namespace tilemix
+
+extern "C" int tm_quant_per_block_int8(const void* x, int64_t x_stride_tok, int64_t x_stride_head,
+                                       const int32_t* cu_seqlens, const int32_t* cu_scale, int batch, int heads,
+                                       int dim, int blk, int max_seqlen, float sm_scale, int8_t* out,
+                                       int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32,
+                                       void* scale_f16, void* stream) {
+  if (x == nullptr || out == nullptr || cu_seqlens == nullptr || cu_scale == nullptr) return TM_ERR_NULL;
+  if (batch < 0 || heads <= 0 || dim <= 0 || blk <= 0 || max_seqlen < 0) return TM_ERR_SHAPE;
+  if ((dim & 7) != 0) return TM_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0 || (x_stride_tok & 7) != 0 || (x_stride_head & 7) != 0)
+    return TM_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0 || (out_stride_tok & 7) != 0 || (out_stride_head & 7) != 0)
+    return TM_ERR_ALIGN;
+  if (batch == 0 || max_seqlen == 0) return TM_OK;
+  const int nblk = (max_seqlen + blk - 1) / blk;
+  if (heads > 65535 || batch > 65535) return TM_ERR_SHAPE;
+  dim3 grid(nblk, heads, batch);
+  tilemix::quant_per_block_int8_kernel<<<grid, tilemix::kQuantThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, dim, blk, sm_scale,
+      out, out_stride_tok, out_stride_head, scale_f32, static_cast<__half*>(scale_f16));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
+}
