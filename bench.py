@@ -1,0 +1,459 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 TileMix hot path: routed FP16/INT8 flash attention.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+Workload (the reference's headline attention configuration): 8 sequences x
+4096 tokens, 24 query heads / 8 KV heads (Llama-3.2-3B), head_dim 128, fp16
+Q/K/V ~ N(0, 1) with 4 outlier channels per (tensor, head) scaled x20 on Q and
+K, causal, SpTrans routing at 50% INT8, tiles (128, 64, 64). A *step* is one
+forward over the batch: per-block INT8 quantisation of K, then the fused
+attention kernel (Q is quantised inside it); the routing map is built once
+beforehand, as the model integration caches it.
+
+One process per GPU (torchrun for N > 1). Sharding is over independent
+(sequence x KV-head) units with no collective: every rank runs its own full
+batch (weak scaling) and ``value`` is the FLOPs of all ranks divided by the
+slowest rank's time. Rank 0 prints one JSON line.
+
+``--impl reference`` times the CPU restatement of the reference's kernels (the
+oracle, bit-exact with the reference run under the Triton interpreter) on the
+host cores, on a bounded sample of the same workload; under torchrun only
+rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime as _dt
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+METRIC = "attention TFLOP/s (SpTrans50, 8x4096, Llama-3.2-3B heads)"
+UNIT = "TFLOP/s"
+CFG = dict(batch=8, seq_len=4096, heads_q=24, heads_k=8, head_dim=128, outliers=4, outlier_scale=20.0,
+           pattern="sptrans", percentage=0.5, block_m=128, block_n=64, block_n_mask=64)
+FALLBACK_PEAKS = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
+
+
+def config_dict(n_gpus: int) -> dict:
+    c = CFG
+    return {
+        "workload": "attention op, config 2: 8 x 4096 tokens, 24 q / 8 kv heads, head_dim 128, causal, "
+                    "sptrans 50% INT8, tiles (128, 64, 64), 4 outlier channels x20",
+        "batch": c["batch"], "seq_len": c["seq_len"], "heads_q": c["heads_q"], "heads_k": c["heads_k"],
+        "head_dim": c["head_dim"], "pattern": c["pattern"], "int8_percentage": c["percentage"],
+        "block_m": c["block_m"], "block_n": c["block_n"], "block_n_mask": c["block_n_mask"],
+        "parallelism": f"shard{n_gpus}: every GPU runs its own batch of 64 (sequence x KV-head) units, "
+                       "no collective",
+        "l2": "inputs larger than L2: each step reads Q, K, V (335 MB) and writes O and K8 (235 MB); no flush",
+    }
+
+
+def attention_flops() -> float:
+    c = CFG
+    T = c["seq_len"]
+    return float(4 * c["head_dim"] * c["heads_q"] * c["batch"] * T * (T + 1) // 2)
+
+
+def make_inputs(seed: int):
+    """Seeded fp16 inputs of the workload, packed token-major [B*T, H, D] on the CPU."""
+    import torch
+
+    c = CFG
+    g = torch.Generator().manual_seed(seed)
+    n = c["batch"] * c["seq_len"]
+    q = torch.randn((n, c["heads_q"], c["head_dim"]), generator=g).to(torch.float16)
+    k = torch.randn((n, c["heads_k"], c["head_dim"]), generator=g).to(torch.float16)
+    v = torch.randn((n, c["heads_k"], c["head_dim"]), generator=g).to(torch.float16)
+    for t, heads in ((q, c["heads_q"]), (k, c["heads_k"])):
+        for h in range(heads):
+            ch = torch.randperm(c["head_dim"], generator=g)[: c["outliers"]]
+            t[:, h, ch] = (t[:, h, ch].float() * c["outlier_scale"]).to(torch.float16)
+    return q, k, v
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profiled_traffic(kernel_tag: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    p = REPO / "profiles" / f"{kernel_tag}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def int8_share(words, block_m: int, block_n: int, block_n_mask: int, T: int) -> float:
+    """Executed INT8 share of the QK tile work of one KV head under the map (causal)."""
+    group = block_n_mask // block_n
+    tot = int8 = 0
+    n_tiles = (T + block_n - 1) // block_n
+    for r, w in enumerate(words):
+        n = min(n_tiles, ((r + 1) * block_m + block_n - 1) // block_n)
+        for t in range(n):
+            tot += 1
+            int8 += (int(w) >> (t // group)) & 1
+    return int8 / tot if tot else 0.0
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.window = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.6)
+        except OSError:
+            self.proc = None
+
+    def mark(self, t0: float, t1: float):
+        self.window = (t0, t1)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "nvidia-smi unavailable"}
+        time.sleep(0.15)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = []
+        for line in out.splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                ts = _dt.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[1]), float(parts[2]), parts[3:7]))
+            except ValueError:
+                continue
+        inside = [r for r in rows if self.window and self.window[0] <= r[0] <= self.window[1]]
+        used = inside or rows
+        reasons = sorted({self.REASONS[i] for r in used for i, s in enumerate(r[3]) if s.lower() == "active"})
+        return {
+            "sm_mhz": statistics.median([r[1] for r in used]) if used else None,
+            "sm_max_mhz": max(r[2] for r in used) if used else None,
+            "reasons": reasons,
+            "samples": len(used),
+            "window": "timed region" if inside else "whole run (no sample inside the timed region)",
+        }
+
+
+def gpu_id_for(device_index: int) -> str:
+    import torch
+
+    try:
+        uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+        return uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+    except Exception:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        return vis.split(",")[device_index] if vis else str(device_index)
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle), shared by the cpu_baseline field and --impl reference
+# ---------------------------------------------------------------------------
+def cpu_units(q, k, v, words, n_units: int, step_budget_s: float, rate_flops: float = 0.9e9):
+    """Tasks of one CPU step: n_units (sequence, Q head) units of the workload, each
+    restricted to evenly spread query blocks so that a unit takes about step_budget_s."""
+    import numpy as np
+    from oracle.cpu_sample import causal_block_flops
+
+    c = CFG
+    T, bm, D = c["seq_len"], c["block_m"], c["head_dim"]
+    nblk = (T + bm - 1) // bm
+    full = sum(causal_block_flops(b, bm, D, T) for b in range(nblk))
+    want = step_budget_s * rate_flops
+    count = nblk if want >= full else max(1, int(round(nblk * want / full)))
+    blocks = sorted({int(x) for x in np.linspace(0, nblk - 1, count).round()})
+    group = c["heads_q"] // c["heads_k"]
+    words_np = np.asarray(words, dtype=np.uint64)
+    tasks, flops = [], 0.0
+    for i in range(n_units):
+        b = i % c["batch"]
+        hq = (i // c["batch"]) % c["heads_q"]
+        hk = hq // group
+        sl = slice(b * T, (b + 1) * T)
+        tasks.append((q[sl, hq:hq + 1].copy(), k[sl, hk:hk + 1].copy(), v[sl, hk:hk + 1].copy(), words_np, blocks,
+                      bm, c["block_n"], c["block_n_mask"]))
+        flops += sum(causal_block_flops(x, bm, D, T) for x in blocks)
+    sample = (f"{n_units} (sequence, Q head) units of the workload, {len(blocks)} of {nblk} query blocks each "
+              f"(spread over the causal triangle), Q/K quantisation included")
+    return tasks, flops, sample
+
+
+def oracle_map_words():
+    from oracle.precision_maps_oracle import make_precision_bitmask
+
+    c = CFG
+    return make_precision_bitmask(c["seq_len"], c["block_m"], c["block_n_mask"], None, c["percentage"], c["pattern"],
+                                  {"percentage": c["percentage"]}, c["block_n"])
+
+
+def run_reference(args) -> None:
+    """--impl reference: the CPU restatement of the reference's kernels on the host cores."""
+    from oracle.cpu_sample import host_cores, make_pool
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = host_cores()
+    pool = make_pool(cores)
+    try:
+        q, k, v = (t.numpy() for t in make_inputs(0))
+        words = oracle_map_words()
+        budget = min(20.0, max(1.0, 150.0 / max(1, args.steps + args.warmup)))
+        tasks, flops, sample = cpu_units(q, k, v, words, cores, budget)
+        for _ in range(args.warmup):
+            pool.map(run_unit_proxy(), tasks, chunksize=1)
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            pool.map(run_unit_proxy(), tasks, chunksize=1)
+            times.append(time.perf_counter() - t0)
+    finally:
+        pool.close()
+        pool.join()
+    step_s = sum(times) / len(times)
+    value = flops / step_s / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16+int8", "data": "synthetic (seeded N(0,1) with outlier channels)",
+        "config": config_dict(args.gpus), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU restatement of the reference's Triton kernels (bit-exact with them under TRITON_INTERPRET=1), "
+                "numpy, one process per host core",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_unit_proxy():
+    from oracle.cpu_sample import run_unit
+
+    return run_unit
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
+    pool = None
+    if want_cpu:  # the oracle's process pool starts before the first CUDA call
+        from oracle.cpu_sample import host_cores, make_pool
+
+        cpu_cores = host_cores()
+        pool = make_pool(cpu_cores)
+
+    import torch
+    import torch.distributed as dist
+
+    from tilemix_b200.attention import tilemix as tmx
+    from tilemix_b200.attention.precision_maps import make_precision_bitmask
+    from tilemix_b200.attention.tilemix_varlen import tilemix_varlen_attention
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=_dt.timedelta(seconds=180), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    c = CFG
+    B, T, HQ, HK, D = c["batch"], c["seq_len"], c["heads_q"], c["heads_k"], c["head_dim"]
+    bm, bn, bnm = c["block_m"], c["block_n"], c["block_n_mask"]
+    q_cpu, k_cpu, v_cpu = make_inputs(rank)
+    q, k, v = q_cpu.to(dev), k_cpu.to(dev), v_cpu.to(dev)
+    words = make_precision_bitmask(T, bm, bnm, None, c["percentage"], c["pattern"], {"percentage": c["percentage"]},
+                                   bn, device=dev)
+    pm = words.view(torch.int64).repeat(HK).view(torch.uint64)
+    words_host = [int(x) for x in words.view(torch.int64).cpu().numpy().view("uint64")]
+    share = int8_share(words_host, bm, bn, bnm, T)
+    cu = torch.arange(0, (B + 1) * T, T, device=dev, dtype=torch.int32)
+    o = torch.empty_like(q)
+    sm_scale = D ** -0.5
+    thr = tmx.rescale_threshold()
+    scalar = bm == 128 and bn == 64
+
+    def step(ev_a=None, ev_b=None):
+        k8, sk16, cuks = tmx._quantize_k(k, cu, T, 64, equal_len=T)
+        if ev_a is not None:
+            ev_a.record()
+        tmx._launch(q, k, v, o, cu, cu, pm, T, T, k8=k8, sk=sk16, cuks=cuks, block_m=bm, block_n=bn,
+                    block_n_mask=bnm, BLKQ=128, BLKK=64, causal=True, sm_scale=sm_scale,
+                    mode_code=tmx.ROUTING_MODE_MIXED, scalar_scales=scalar, int8_use_fp16_v=True, threshold=thr)
+        if ev_b is not None:
+            ev_b.record()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    if tmx.device_error_code(dev) != 0:
+        raise RuntimeError("attention kernel reported a device-side timeout during warm-up")
+
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(gpu_id_for(local_rank))
+    sampler.start()
+    barrier()
+    t_host0 = time.time()
+    start.record()
+    for i in range(args.steps):
+        step(ev_a[i], ev_b[i])
+    end.record()
+    barrier()
+    t_host1 = time.time()
+    sampler.mark(t_host0, t_host1)
+    clocks = sampler.stop()
+    ms_step = max_over_ranks(start.elapsed_time(end) / args.steps)
+    attn_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(ev_a, ev_b)) / args.steps)
+    if tmx.device_error_code(dev) != 0:
+        raise RuntimeError("attention kernel reported a device-side timeout in the timed region")
+
+    # end to end through the public API: pinned host inputs in, output back to pinned host memory
+    q_pin, k_pin, v_pin = q_cpu.pin_memory(), k_cpu.pin_memory(), v_cpu.pin_memory()
+    out_pin = torch.empty((B, T, HQ, D), dtype=torch.float16).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        qd.copy_(q_pin, non_blocking=True)
+        kd.copy_(k_pin, non_blocking=True)
+        vd.copy_(v_pin, non_blocking=True)
+        out = tilemix_varlen_attention(qd.view(B, T, HQ, D).permute(0, 2, 1, 3),
+                                       kd.view(B, T, HK, D).permute(0, 2, 1, 3),
+                                       vd.view(B, T, HK, D).permute(0, 2, 1, 3), bm, bn, block_n_mask=bnm,
+                                       causal=True, scale=sm_scale, precision_map_all=pm, candidates=[],
+                                       flat_lengths=[])
+        out_pin.copy_(out.permute(0, 2, 1, 3), non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 30))
+    for _ in range(max(3, min(args.warmup, 5))):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    h2d = (q.numel() + k.numel() + v.numel()) * 2
+    d2h = out_pin.numel() * 2
+
+    flops = attention_flops()
+    value = world * flops / (ms_step * 1e-3) / 1e12
+    peaks, peak_src = load_peaks()
+    peak = float(peaks["bf16_tflops"])
+    achieved = flops / (attn_ms * 1e-3) / 1e12
+    int8_peak = 2.0 * peak
+    t_star_ms = flops / 2 * (1 - share) / (peak * 1e12) * 1e3 + flops / 2 * share / (int8_peak * 1e12) * 1e3 \
+        + flops / 2 / (peak * 1e12) * 1e3
+    traffic = profiled_traffic("attn_fwd_paired_config2")
+
+    cpu_line = None
+    if want_cpu:
+        try:
+            tasks, cflops, sample = cpu_units(q_cpu.numpy(), k_cpu.numpy(), v_cpu.numpy(), oracle_map_words(),
+                                              cpu_cores, 8.0)
+            t0 = time.perf_counter()
+            pool.map(run_unit_proxy(), tasks, chunksize=1)
+            dt = time.perf_counter() - t0
+            cpu_line = {"value": cflops / dt / 1e12, "unit": UNIT, "cores": cpu_cores, "kind": "port",
+                        "sample": sample, "seconds": dt}
+        finally:
+            pool.close()
+            pool.join()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16+int8", "data": "synthetic (seeded N(0,1) with outlier channels)",
+            "config": config_dict(world),
+            "roofline": {
+                "bound": "tensor", "kernel": "attn_fwd_paired", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                "peak_source": f"bf16_tflops (burst) of {peak_src}", "kernel_ms": attn_ms,
+                "flops_per_launch": flops,
+                "mixed": {"int8_share": share, "int8_peak_assumed": int8_peak, "t_star_ms": t_star_ms,
+                          "frac": t_star_ms / attn_ms,
+                          "note": "routed FP16/INT8 roofline; INT8 dense peak taken as 2x the measured bf16 peak"},
+            },
+            "cpu_baseline": cpu_line,
+            "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "steps": e2e_steps,
+                    "api": "tilemix_varlen_attention"},
+            "clocks": clocks,
+            "gpu_launches": 2 * args.steps,
+            "rescale_threshold": thr,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the oracle timing on the host cores")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

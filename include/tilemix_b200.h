@@ -53,6 +53,53 @@ int tm_quant_per_block_int8(const void* x, int64_t x_stride_tok, int64_t x_strid
                             int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32,
                             void* scale_f16, void* stream);
 
+/* Routing-map patterns of make_precision_bitmask (attention/precision_maps.py:404-636). */
+#define TM_MAP_ZERO 0
+#define TM_MAP_ONE 1
+#define TM_MAP_BAND 2
+#define TM_MAP_GLOBAL 3
+#define TM_MAP_ROW_RAND 4
+#define TM_MAP_ALIGN_SPARSE 5
+#define TM_MAP_BIGBIRD 6
+#define TM_MAP_SPTRANS 7
+
+/* Arguments of tm_build_precision_map; the names follow the reference's
+ * (seq_len, BLOCK_M, BLOCK_N, COMPUTE_BLOCK_N, percentage, pattern_params). */
+typedef struct tm_map_params {
+  int seq_len;
+  int block_m;         /* BLOCK_M: query rows per map row */
+  int block_n_mask;    /* BLOCK_N: keys per mask group (map column) */
+  int compute_block_n; /* COMPUTE_BLOCK_N: keys per attention tile; divides block_n_mask */
+  int pattern;         /* TM_MAP_* */
+  double percentage;   /* INT8 share of the causal work, in [0, 1]; read for patterns >= TM_MAP_BAND */
+  /* sptrans: stride > 0 (the reference's default is min(128, seq_len / 4)) and
+   * c (default min(32, stride / 4)). */
+  int stride, c;
+  /* global: HOST array of token positions (pattern_params["key_pos"]);
+   * NULL = the reference's default 0 .. min(4, seq_len) - 1. */
+  const int64_t* key_pos;
+  int num_key_pos;
+  /* bigbird: >= 0 each (the reference's defaults are 2 and 3). */
+  int num_global_block, num_rand_block;
+} tm_map_params;
+
+/*
+ * Routing map on the GPU: out[r] bit j = 1 routes (query block r, mask group
+ * j) to INT8, 0 to FP16. Replaces make_precision_bitmask
+ * (attention/precision_maps.py:404-636) for token_mask = None — the path of
+ * the model integration (models/tilemix_llama.py:333-364) — bit for bit,
+ * including its seeded draws (torch's CPU generator, seed 42: the global
+ * generator for row_rand / bigbird, a private one for the weighted retarget).
+ *   out         device uint64 [ceil(seq_len / block_m)]
+ *   error_flag  optional device int; set to 1 when the weighted retarget ends
+ *               farther from its target than one mask-group weight (where the
+ *               reference raises RuntimeError, :319-325)
+ * Limits: ceil(seq_len / block_n_mask) <= 64 (the reference's own limit,
+ * TM_ERR_SHAPE); at most 4096 map rows and 65536 cells (TM_ERR_UNSUPPORTED).
+ * One CTA, no device memory besides `out` and `error_flag`.
+ */
+int tm_build_precision_map(const tm_map_params* params, uint64_t* out, int* error_flag, void* stream);
+
 /*
  * Arguments of the fused mixed-precision attention forward.
  * Mirrors the launch of attn_fwd in launch_prequantized

@@ -106,11 +106,12 @@ def _softmax_prefix_update(qk16, m_i, l_i, acc):
 def attn_fwd(q, k, v, cu_q, cu_k, bitmask, *, q8=None, sq=None, cu_qs=None, k8=None, sk=None, cu_ks=None,
              v8=None, sv=None, cu_vs=None, max_seqlen_q, max_seqlen_k, block_m=128, block_n=64,
              block_n_mask=None, BLKQ=128, BLKK=64, causal=False, sm_scale=None, routing_mode=ROUTING_MODE_MIXED,
-             scalar_scales=True, int8_use_fp16_v=False, bias=None, heads=None):
+             scalar_scales=True, int8_use_fp16_v=False, bias=None, heads=None, q_blocks=None):
     """Reference attention forward on packed [tokens, heads, D] fp16 arrays.
 
-    ``heads`` optionally restricts the computed Q heads (others stay zero), for
-    bounded CPU samples. Returns fp16 [tokens, HQ, D].
+    ``heads`` and ``q_blocks`` optionally restrict the computed Q heads and
+    query blocks (others stay zero), for bounded CPU samples. Returns fp16
+    [tokens, HQ, D].
     """
     q = np.asarray(q, dtype=f16)
     k = np.asarray(k, dtype=f16)
@@ -135,7 +136,7 @@ def attn_fwd(q, k, v, cu_q, cu_k, bitmask, *, q8=None, sq=None, cu_qs=None, k8=N
         Tq, Tk = int(cu_q[z + 1]) - q0, int(cu_k[z + 1]) - k0
         for hq in head_list:
             hk = hq // group if group != 1 else hq                    # :588-592
-            for start_m in range(n_m):
+            for start_m in (range(n_m) if q_blocks is None else q_blocks):
                 if start_m * block_m >= Tq:                           # :600
                     continue
                 n_blocks = (Tk + block_n - 1) // block_n              # :603
@@ -247,7 +248,7 @@ def quantize_qkv_for_tilemix(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, 
 def tilemix_attention_with_quant(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q, max_seqlens_k,
                                  precision_bitmask, *, block_m=128, block_n=64, block_n_mask=None, BLKQ=128,
                                  BLKK=64, causal=False, sm_scale=None, routing_mode="mixed", scalar_scales=True,
-                                 int8_use_fp16_v=False, bias=None, heads=None):
+                                 int8_use_fp16_v=False, bias=None, heads=None, q_blocks=None):
     """tilemix.py:1340-1447 for an explicit routing mode ("mixed" / "fp16" / "int8")."""
     mode = {"mixed": ROUTING_MODE_MIXED, "fp16": ROUTING_MODE_FP16, "int8": ROUTING_MODE_INT8}[routing_mode]
     kw = {}
@@ -263,7 +264,8 @@ def tilemix_attention_with_quant(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen
     return attn_fwd(q, k, v, cu_seqlens_q, cu_seqlens_k, precision_bitmask, max_seqlen_q=max_seqlens_q,
                     max_seqlen_k=max_seqlens_k, block_m=block_m, block_n=block_n, block_n_mask=block_n_mask,
                     BLKQ=BLKQ, BLKK=BLKK, causal=causal, sm_scale=sm_scale, routing_mode=mode,
-                    scalar_scales=scalar_scales, int8_use_fp16_v=int8_use_fp16_v, bias=bias, heads=heads, **kw)
+                    scalar_scales=scalar_scales, int8_use_fp16_v=int8_use_fp16_v, bias=bias, heads=heads,
+                    q_blocks=q_blocks, **kw)
 
 
 def attention_flops(cu_seqlens_q, heads_q: int, head_dim: int, causal: bool = True) -> float:

@@ -56,6 +56,17 @@ class TmAttnTuning(ctypes.Structure):
     _fields_ = [("rescale_threshold", ctypes.c_float), ("force_general", c_int)]
 
 
+class TmMapParams(ctypes.Structure):
+    """Mirror of ``tm_map_params`` (include/tilemix_b200.h)."""
+
+    _fields_ = [
+        ("seq_len", c_int), ("block_m", c_int), ("block_n_mask", c_int), ("compute_block_n", c_int),
+        ("pattern", c_int), ("percentage", ctypes.c_double), ("stride", c_int), ("c", c_int),
+        ("key_pos", ctypes.POINTER(c_i64)), ("num_key_pos", c_int),
+        ("num_global_block", c_int), ("num_rand_block", c_int),
+    ]
+
+
 # (name, restype, argtypes) of every exported entry point.
 SIGNATURES = {
     "tm_quant_per_block_int8": (c_int, [c_void_p, c_i64, c_i64, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
@@ -63,6 +74,7 @@ SIGNATURES = {
                                         c_void_p]),
     "tm_attn_fwd": (c_int, [ctypes.POINTER(TmAttnParams), c_void_p]),
     "tm_attn_fwd_ex": (c_int, [ctypes.POINTER(TmAttnParams), ctypes.POINTER(TmAttnTuning), c_void_p]),
+    "tm_build_precision_map": (c_int, [ctypes.POINTER(TmMapParams), c_void_p, c_void_p, c_void_p]),
     "tm_status_string": (ctypes.c_char_p, [c_int]),
 }
 
@@ -78,11 +90,13 @@ def lib() -> ctypes.CDLL:
                 f"tilemix_b200 native library not found at {LIB_PATH}; build it with "
                 "`python -m tilemix_b200.build` (no CPU fallback exists)")
         handle = ctypes.CDLL(str(LIB_PATH))
+        missing = [name for name in SIGNATURES if not hasattr(handle, name)]
+        if missing:
+            raise RuntimeError(f"{LIB_PATH} lacks {missing}; rebuild it with `python -m tilemix_b200.build --force`")
         for name, (res, args) in SIGNATURES.items():
-            if hasattr(handle, name):
-                fn = getattr(handle, name)
-                fn.restype = res
-                fn.argtypes = args
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
         _LIB = handle
     return _LIB
 

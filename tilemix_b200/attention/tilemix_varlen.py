@@ -1,0 +1,87 @@
+"""Batched-head entry point used by the model attention layers (drop-in for the
+reference's ``attention/tilemix_varlen.py:17-96``).
+
+``tilemix_varlen_attention`` takes ``[B, H, T, D]`` tensors, packs them
+token-major (a no-op when they are permuted views of token-major data, as the
+Llama/Qwen prefill produces), builds equal-length ``cu_seqlens`` and runs the
+routed attention with the reference's fixed settings (``BLKQ=128``,
+``BLKK=64``, ``scalar_scales = block_m == 128 and block_n == 64``, routing
+mode from ``TILEMIX_BITMASK_ROUTING_MODE``, FP16 V from
+``TILEMIX_SCORE_ONLY_PV``). Because every sequence has length T, the K scale
+offsets are computed without a device-to-host read, so the call never
+synchronises the host.
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from tilemix_b200.attention.tilemix import _attention_forward, _routing_mode_code, _validate
+
+
+def _env_flag(name: str, default: str = "0") -> bool:
+    return (os.getenv(name) or default).strip().lower() not in ("0", "false", "no", "")
+
+
+def tilemix_varlen_attention(q: Tensor, k: Tensor, v: Tensor, block_m: int, block_n: int, *,
+                             block_n_mask: Optional[int] = None, causal: bool, scale: float,
+                             precision_map_all: Tensor, candidates: list[tuple[int, int]],
+                             flat_lengths: list[int], bias: Optional[Tensor] = None) -> Tensor:
+    """Routed FP16/INT8 attention of ``[B, H, T, D]`` q/k/v; returns ``[B, Hq, T, D]``.
+
+    ``candidates`` and ``flat_lengths`` are accepted for signature parity and
+    unused, as in the reference.
+    """
+    B, Hq, Tq, D = q.shape
+    _, Hk, Tk, Dk = k.shape
+    _, Hv, Tv, Dv = v.shape
+    assert Dk == D
+    assert Dv == D
+    assert Hk == Hv, "K and V must have the same number of heads (GQA support)"
+
+    Q = q.permute(0, 2, 1, 3).reshape(B * Tq, Hq, D).contiguous()
+    K = k.permute(0, 2, 1, 3).reshape(B * Tk, Hk, D).contiguous()
+    V = v.permute(0, 2, 1, 3).reshape(B * Tk, Hv, D).contiguous()
+    device = Q.device
+    cu_q = torch.arange(0, (B + 1) * Tq, Tq, device=device, dtype=torch.int32)
+    cu_k = torch.arange(0, (B + 1) * Tk, Tk, device=device, dtype=torch.int32)
+
+    pm = precision_map_all
+    assert pm.dtype == torch.uint64, f"precision_map dtype must be uint64, got {pm.dtype}"
+    if block_n_mask is None:
+        block_n_mask = block_n
+    if block_n_mask % block_n != 0:
+        raise ValueError(f"block_n_mask ({block_n_mask}) must be a multiple of block_n ({block_n})")
+    if Tq != Tk:
+        raise ValueError(f"Tq ({Tq}) != Tk ({Tk}). Bitmask was created assuming they're equal. "
+                         f"This will cause incorrect indexing in the kernel.")
+    m_blocks_total = (Tq + block_m - 1) // block_m
+    n_mask_blocks_total = (Tk + block_n_mask - 1) // block_n_mask
+    if n_mask_blocks_total > 64:
+        raise ValueError(f"64-bit precision mask requires n_mask_blocks<=64, got n_mask_blocks={n_mask_blocks_total} "
+                         f"(Tk={Tk}, block_n_mask={block_n_mask})")
+    expected_pm_elems = Hk * m_blocks_total
+    assert pm.numel() == expected_pm_elems, (
+        f"precision_map length mismatch: got {pm.numel()}, expected {expected_pm_elems} "
+        f"(Hk={Hk} KV heads × m_blocks={m_blocks_total}, n_mask_blocks={n_mask_blocks_total})")
+    if bias is not None:
+        bias = bias.to(device=device, dtype=q.dtype).contiguous()
+        if bias.shape != (B, Hq, Tq, Tk):
+            raise ValueError(f"Bias shape mismatch: got {bias.shape}, expected {(B, Hq, Tq, Tk)}")
+
+    routing_mode = (os.getenv("TILEMIX_BITMASK_ROUTING_MODE") or "mixed").strip().lower()
+    if routing_mode == "auto":
+        from tilemix_b200.attention.tilemix import classify_bitmask_routing
+        routing_mode = classify_bitmask_routing(pm, seqlen_q=Tq, seqlen_k=Tk, block_m=block_m, block_n=block_n,
+                                                block_n_mask=block_n_mask, causal=causal)
+    _routing_mode_code(routing_mode)
+    scalar_scales = block_m == 128 and block_n == 64
+    _validate(Q, K, V, Tq, Tk, pm, block_m, block_n, block_n_mask, 128, 64, scalar_scales)
+    out = _attention_forward(Q, K, V, cu_q, cu_k, Tq, Tk, pm, block_m=block_m, block_n=block_n,
+                             block_n_mask=block_n_mask, BLKQ=128, BLKK=64, causal=causal, sm_scale=scale,
+                             mode=routing_mode, scalar_scales=scalar_scales,
+                             int8_use_fp16_v=_env_flag("TILEMIX_SCORE_ONLY_PV", "1"), bias=bias, equal_len=Tq)
+    return out.view(B, Tq, Hq, D).permute(0, 2, 1, 3)

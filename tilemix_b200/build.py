@@ -20,7 +20,8 @@ INCLUDE = REPO_DIR / "include"
 LIB_NAME = "libtilemix_b200.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["attn_api.cu", "attn_fwd_general.cu", "attn_fwd_paired.cu", "attn_fwd_persistent.cu", "quant.cu", "precision_map.cu"]
+SOURCES = ["attn_api.cu", "attn_fwd_general.cu", "attn_fwd_paired.cu", "attn_fwd_persistent.cu", "quant.cu",
+           "precision_map.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -51,7 +52,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     """Compile every CUDA source into ``tilemix_b200/libtilemix_b200.so``."""
     if not force and not _stale():
         return LIB_PATH
-    srcs = [str(CSRC / s) for s in SOURCES if (CSRC / s).exists()]
+    srcs = [str(CSRC / s) for s in SOURCES]
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [_nvcc(), *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-shared", "-o", str(tmp), *srcs]
     res = subprocess.run(cmd, capture_output=True, text=True)
