@@ -46,15 +46,19 @@ FALLBACK_PEAKS = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=
 
 def config_dict(n_gpus: int) -> dict:
     c = CFG
+    tokens = c["batch"] * c["seq_len"]
+    rd = tokens * (c["heads_q"] + 2 * c["heads_k"]) * c["head_dim"] * 2
+    wr = tokens * (2 * c["heads_q"] + c["heads_k"]) * c["head_dim"]
     return {
-        "workload": "attention op, config 2: 8 x 4096 tokens, 24 q / 8 kv heads, head_dim 128, causal, "
-                    "sptrans 50% INT8, tiles (128, 64, 64), 4 outlier channels x20",
+        "workload": f"attention op, config 2: {c['batch']} x {c['seq_len']} tokens, 24 q / 8 kv heads, head_dim 128, "
+                    "causal, sptrans 50% INT8, tiles (128, 64, 64), 4 outlier channels x20",
         "batch": c["batch"], "seq_len": c["seq_len"], "heads_q": c["heads_q"], "heads_k": c["heads_k"],
         "head_dim": c["head_dim"], "pattern": c["pattern"], "int8_percentage": c["percentage"],
         "block_m": c["block_m"], "block_n": c["block_n"], "block_n_mask": c["block_n_mask"],
-        "parallelism": f"shard{n_gpus}: every GPU runs its own batch of 64 (sequence x KV-head) units, "
-                       "no collective",
-        "l2": "inputs larger than L2: each step reads Q, K, V (335 MB) and writes O and K8 (235 MB); no flush",
+        "parallelism": f"shard{n_gpus}: every GPU runs its own batch of {c['batch'] * c['heads_k']} "
+                       "(sequence x KV-head) units, no collective",
+        "l2": f"inputs larger than L2 (126 MB): each step reads Q, K, V ({rd / 1e6:.0f} MB) and writes O and K8 "
+              f"({wr / 1e6:.0f} MB); no flush",
     }
 
 
@@ -446,7 +450,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the oracle timing on the host cores")
+    ap.add_argument("--batch", type=int, default=CFG["batch"],
+                    help="sequences per GPU (default: the workload's 8; smaller only for profiling captures)")
     args = ap.parse_args()
+    CFG["batch"] = args.batch
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":

@@ -52,6 +52,25 @@ static int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, in
   return r == CUDA_SUCCESS ? TM_OK : TM_ERR_TMAP;
 }
 
+// 4-D map over a packed fp16 [tokens, heads, 128] tensor that fetches all 128
+// dims of `box_rows` tokens in one copy: dims {64 (d low), tokens, 2 (d high),
+// heads}, box {64, box_rows, 2, 1}. In shared memory the box lands as two
+// [box_rows x 128 B] halves (dims 0-63, then 64-127), the K-major SW128
+// operand layout of the tcgen05 kernels.
+static int make_map_d128(CUtensorMap* m, const void* base, int heads, int64_t tokens, int64_t stride_head,
+                         int64_t stride_tok, int box_rows) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return TM_ERR_LAUNCH;
+  cuuint64_t dims[4] = {64u, static_cast<cuuint64_t>(tokens), 2u, static_cast<cuuint64_t>(heads)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(stride_tok * 2), 128u, static_cast<cuuint64_t>(stride_head * 2)};
+  cuuint32_t box[4] = {64u, static_cast<cuuint32_t>(box_rows), 2u, 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TM_OK : TM_ERR_TMAP;
+}
+
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace tilemix
@@ -152,13 +171,23 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   if (p->heads_q > 65535 || p->batch > 65535) return TM_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool paired_ok = !force_general && D == 128 && p->block_m == 128 && (fuse_q || !need_int8);
-  if (paired_ok) {
+  if (paired_ok && kernel_choice == 2) {
     CUtensorMap m_q;
     rc = make_map(&m_q, p->q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, p->heads_q, p->q_tokens, p->q_stride_head,
                   p->q_stride_tok, 64, CU_TENSOR_MAP_SWIZZLE_128B, 128);
     if (rc != TM_OK) return rc;
-    if (kernel_choice == 2) return launch_attn_persistent(m_q, m_k16, m_k8, m_v, a, p->batch, p->max_seqlen_q, st);
-    return launch_attn_paired(m_q, m_k16, m_k8, m_v, a, p->batch, p->max_seqlen_q, st);
+    return launch_attn_persistent(m_q, m_k16, m_k8, m_v, a, p->batch, p->max_seqlen_q, st);
+  }
+  if (paired_ok) {
+    // The paired kernel fetches all 128 dims of a tile in one 4-D copy.
+    CUtensorMap q4, k4, v4;
+    rc = make_map_d128(&q4, p->q, p->heads_q, p->q_tokens, p->q_stride_head, p->q_stride_tok, 128);
+    if (rc != TM_OK) return rc;
+    rc = make_map_d128(&k4, p->k, p->heads_k, p->k_tokens, p->k_stride_head, p->k_stride_tok, 64);
+    if (rc != TM_OK) return rc;
+    rc = make_map_d128(&v4, p->v, p->heads_k, p->k_tokens, p->v_stride_head, p->v_stride_tok, 64);
+    if (rc != TM_OK) return rc;
+    return launch_attn_paired(q4, k4, m_k8, v4, a, p->batch, p->max_seqlen_q, st);
   }
   const int tiles = (p->max_seqlen_q + 127) / 128;
   return launch_attn_general(m_k16, m_k8, m_v, a, tiles, p->heads_q, p->batch, st);

@@ -203,6 +203,33 @@ __device__ __forceinline__ int route_kind(int mode, uint64_t bits, int j, int bl
   return static_cast<int>((bits >> ((j * kKeys) / block_n_mask)) & 1ull);
 }
 
+// Route of the consecutive 64-key tiles j = 0, 1, 2, ... of one query tile,
+// the same as route_kind(mode, bits, j, block_n_mask) but with the mask group
+// index j / (block_n_mask / 64) tracked incrementally instead of divided out
+// per tile. Call kind() for tile j, then advance() to move to tile j + 1.
+struct RouteWalker {
+  uint64_t bits;
+  int mode, per, grp, sub;
+  __device__ __forceinline__ void init(int mode_, uint64_t bits_, int block_n_mask) {
+    mode = mode_;
+    bits = bits_;
+    per = block_n_mask / kKeys;
+    grp = 0;
+    sub = 0;
+  }
+  __device__ __forceinline__ int kind() const {
+    if (mode == 1) return 0;  // TM_ROUTE_FP16
+    if (mode == 2) return 1;  // TM_ROUTE_INT8
+    return grp < 64 ? static_cast<int>((bits >> grp) & 1ull) : 0;
+  }
+  __device__ __forceinline__ void advance() {
+    if (++sub == per) {
+      sub = 0;
+      ++grp;
+    }
+  }
+};
+
 // Number of 64-key tiles the reference visits for the query rows
 // [row0, row0 + rows) of a sequence (tilemix.py:603-612), in 64-key units.
 __device__ __forceinline__ int visited_key_tiles(int row0, int rows, int seqlen_q, int seqlen_k, int causal) {

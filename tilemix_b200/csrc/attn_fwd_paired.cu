@@ -12,8 +12,13 @@
 //                     TMEM lane). At start: scale Q in place in shared memory
 //                     (fp16(q * sm_scale * log2e)) and quantise it per 128-row
 //                     block into the INT8 operand (BLKQ = 128 block = the tile).
-//   warp 8            TMA producer: Q tiles, then K (only the formats routed by
-//                     either tile) and V tiles of 64 keys, 3-stage ring.
+//   warp 8            TMA producer of K (only the formats routed by either tile),
+//                     64 keys per stage of a 3-stage ring
+//   warp 10           TMA producer of the Q tiles, then of V (same ring stages)
+//                     Every K16 / V / Q tile arrives in a single 4-D copy (all 128
+//                     dims), so each producer issues at most two copies per stage:
+//                     a thread's bulk-tensor copies go out one after another, and
+//                     splitting K and V over two warps halves that serial chain.
 //   warp 9            MMA issuer: S_X = Q_X K^T (tcgen05 kind::f16 or kind::i8,
 //                     both operands in shared memory) into a TMEM score slot of
 //                     tile X; O_X += P_X V (kind::f16, P from TMEM, fp32 O).
@@ -30,8 +35,11 @@ namespace paired {
 constexpr int kD = 128;
 constexpr int kRows = 128;
 constexpr int kStages = 3;
-constexpr int kPrefetch = 8;  // key tiles warmed in L2 ahead of the TMA ring
-constexpr int kThreads = 320;
+#ifndef TILEMIX_PAIRED_PREFETCH
+#define TILEMIX_PAIRED_PREFETCH 0
+#endif
+constexpr int kPrefetch = TILEMIX_PAIRED_PREFETCH;  // key tiles warmed in L2 ahead of the ring (0 = off)
+constexpr int kThreads = 352;
 constexpr uint32_t kTmemCols = 512;
 
 constexpr uint32_t kQ16Bytes = kRows * kD * 2;  // 32 KB, two 64-column boxes of 16 KB
@@ -48,7 +56,8 @@ constexpr uint32_t kOffBar = kOffK8 + kStages * kK8Bytes;
 constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
 
 struct Barriers {
-  uint64_t full[kStages];
+  uint64_t full_k[kStages];
+  uint64_t full_v[kStages];
   uint64_t empty[kStages];
   uint64_t q_full[2];
   uint64_t q_ready[2];
@@ -114,7 +123,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->full_k[s], 1);
+      mbar_init(&bars->full_v[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
     for (int x = 0; x < 2; ++x) {
@@ -138,164 +148,160 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tbase = bars->tmem_base;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tmap(&tm_q);
+  if (warp == 8 || warp == 10) {
+    // ------------------------------------------------------------------ producers
+    // The whole warp runs the loop (warp-uniform control flow); one elected
+    // lane issues each copy.
+    const bool is_k = warp == 8;
+    if (is_k) {
       prefetch_tmap(&tm_k16);
-      prefetch_tmap(&tm_v);
       if (a.mode != TM_ROUTE_FP16) prefetch_tmap(&tm_k8);
+    } else {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_v);
+#pragma unroll
       for (int x = 0; x < 2; ++x) {
         if (tl[x].mtile * kRows >= seqlen_q) continue;
-        mbar_arrive_expect_tx(&bars->q_full[x], kQ16Bytes);
-        for (int box = 0; box < 2; ++box)
-          tma_load_3d(smem + kOffQ16 + x * kQ16Bytes + box * (kQ16Bytes / 2), &tm_q, &bars->q_full[x], box * 64,
-                      tl[x].hq, q_start + tl[x].mtile * kRows);
+        mbar_arrive_expect_tx_e(&bars->q_full[x], kQ16Bytes);
+        tma_load_4d_e(smem + kOffQ16 + x * kQ16Bytes, &tm_q, &bars->q_full[x], 0, q_start + tl[x].mtile * kRows, 0,
+                      tl[x].hq);
       }
-      bool ok = true;
-      for (int j = 0; j < n_iter && ok; ++j) {
-        const int s = j % kStages;
-        if (j >= kStages) ok = mbar_wait(&bars->empty[s], ((j - kStages) / kStages) & 1, a.err, kErrTimeoutEmpty);
-        if (!ok) break;
+    }
+    bool ok = true;
+    RouteWalker rw[2];
+#pragma unroll
+    for (int x = 0; x < 2; ++x) rw[x].init(a.mode, tl[x].bits, a.block_n_mask);
+    for (int j = 0; j < n_iter && ok; ++j) {
+      const int s = j % kStages;
+      if (j >= kStages)
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&bars->empty[s], ((j - kStages) / kStages) & 1, a.err, kErrTimeoutEmpty));
+      if (!ok) break;
+      const int tok = k_start + j * kKeys;
+      if (is_k) {
         bool n16 = false, n8 = false;
+#pragma unroll
         for (int x = 0; x < 2; ++x) {
           if (j < tl[x].nb) {
-            if (route_kind(a.mode, tl[x].bits, j, a.block_n_mask))
+            if (rw[x].kind())
               n8 = true;
             else
               n16 = true;
           }
+          rw[x].advance();
         }
-        const uint32_t bytes = kVBytes + (n16 ? kK16Bytes : 0u) + (n8 ? kK8Bytes : 0u);
-        mbar_arrive_expect_tx(&bars->full[s], bytes);
-        const int tok = k_start + j * kKeys;
-        for (int box = 0; box < 2; ++box) {
-          if (n16)
-            tma_load_3d(smem + kOffK16 + s * kK16Bytes + box * (kK16Bytes / 2), &tm_k16, &bars->full[s], box * 64,
-                        hk, tok);
-          tma_load_3d(smem + kOffV + s * kVBytes + box * (kVBytes / 2), &tm_v, &bars->full[s], box * 64, hk, tok);
-        }
-        if (n8) tma_load_3d(smem + kOffK8 + s * kK8Bytes, &tm_k8, &bars->full[s], 0, hk, tok);
-        // Every CTA of this KV head walks the keys at the same pace, so a tile
-        // that misses L2 misses for all of them: warm L2 kPrefetch tiles ahead.
-        const int jp = (j == 0) ? 1 : j + kPrefetch;
-        for (int jq = jp; jq <= j + kPrefetch && jq < n_iter; ++jq) {
-          bool p16 = false, p8 = false;
-          for (int x = 0; x < 2; ++x) {
-            if (jq < tl[x].nb) {
-              if (route_kind(a.mode, tl[x].bits, jq, a.block_n_mask))
-                p8 = true;
-              else
-                p16 = true;
-            }
-          }
+        mbar_arrive_expect_tx_e(&bars->full_k[s], (n16 ? kK16Bytes : 0u) + (n8 ? kK8Bytes : 0u));
+        if (n16) tma_load_4d_e(smem + kOffK16 + s * kK16Bytes, &tm_k16, &bars->full_k[s], 0, tok, 0, hk);
+        if (n8) tma_load_3d_e(smem + kOffK8 + s * kK8Bytes, &tm_k8, &bars->full_k[s], 0, hk, tok);
+      } else {
+        mbar_arrive_expect_tx_e(&bars->full_v[s], kVBytes);
+        tma_load_4d_e(smem + kOffV + s * kVBytes, &tm_v, &bars->full_v[s], 0, tok, 0, hk);
+      }
+      if (kPrefetch > 0 && lane == 0) {
+        const int jq = j + kPrefetch;
+        if (jq < n_iter) {
           const int ptok = k_start + jq * kKeys;
-          for (int box = 0; box < 2; ++box) {
-            if (p16) tma_prefetch_l2_3d(&tm_k16, box * 64, hk, ptok);
-            tma_prefetch_l2_3d(&tm_v, box * 64, hk, ptok);
+          if (is_k) {
+            tma_prefetch_l2_4d(&tm_k16, 0, ptok, 0, hk);
+            if (a.mode != TM_ROUTE_FP16) tma_prefetch_l2_3d(&tm_k8, 0, hk, ptok);
+          } else {
+            tma_prefetch_l2_4d(&tm_v, 0, ptok, 0, hk);
           }
-          if (p8) tma_prefetch_l2_3d(&tm_k8, 0, hk, ptok);
         }
       }
-      const int first = max(0, n_iter - kStages);
-      for (int j = first; j < n_iter; ++j)
-        mbar_wait(&bars->full[j % kStages], (j / kStages) & 1, a.err, kErrTimeoutDrain);
+    }
+    // Drain: every copy this warp issued has landed before the CTA can exit.
+    const int first = max(0, n_iter - kStages);
+    for (int j = first; j < n_iter; ++j)
+      mbar_wait(is_k ? &bars->full_k[j % kStages] : &bars->full_v[j % kStages], (j / kStages) & 1, a.err,
+                kErrTimeoutDrain);
+    if (!is_k)
       for (int x = 0; x < 2; ++x)
         if (tl[x].mtile * kRows < seqlen_q) mbar_wait(&bars->q_full[x], 0, a.err, kErrTimeoutDrain);
-    }
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA issuer
-    // Event loop: each tile X is an independent stream of S(j) and PV(j)
-    // launches; whichever launch has its inputs ready is issued, so neither
-    // tile nor the TMA ring blocks the other's work.
-    if (lane == 0) {
-      const uint32_t idesc_qk16 = make_idesc(1, 0, 0, 0, 128, 64);
-      const uint32_t idesc_qk8 = make_idesc(2, 1, 0, 0, 128, 64);
-      const uint32_t idesc_pv = make_idesc(1, 0, 0, 1, 128, kD);
-      bool ok = true;
-      for (int x = 0; x < 2 && ok; ++x)
-        if (tl[x].mtile * kRows < seqlen_q) ok = mbar_wait(&bars->q_ready[x], 0, a.err, kErrTimeoutQ);
-      tc_fence_after();
-      int s_next[2] = {0, 0};
-      int pv_next[2] = {0, 0};
-      int released = 0;
-      unsigned long long t_last = globaltimer_ns();
-      while (ok) {
-        bool progress = false;
+    // Fixed issue order per key tile j, run by the whole warp with one elected
+    // lane issuing:   S_A(j), S_B(j), PV_A(j-1), PV_B(j-1), release stage j-1.
+    // Every wait is on the input the next group needs, so the tensor core
+    // always has the previous groups queued. S_X(j) overwrites TMEM slot j&1,
+    // which P_X(j-2) occupied: PV_X(j-2) was issued earlier by this thread and
+    // tcgen05.mma operations from one thread execute in issue order, so it has
+    // read P before S_X(j) writes the slot.
+    // Descriptors are built once; a byte offset is added as offset >> 4 to the
+    // start-address field (all shared-memory offsets here are < 256 KB).
+    constexpr uint32_t idesc_qk16 = make_idesc(1, 0, 0, 0, 128, 64);
+    constexpr uint32_t idesc_qk8 = make_idesc(2, 1, 0, 0, 128, 64);
+    constexpr uint32_t idesc_pv = make_idesc(1, 0, 0, 1, 128, kD);
+    const uint64_t dq16 = make_sdesc(smem_u32(smem + kOffQ16), 16, 1024, 2);
+    const uint64_t dq8 = make_sdesc(smem_u32(smem + kOffQ8), 16, 1024, 2);
+    const uint64_t dk16 = make_sdesc(smem_u32(smem + kOffK16), 16, 1024, 2);
+    const uint64_t dk8 = make_sdesc(smem_u32(smem + kOffK8), 16, 1024, 2);
+    const uint64_t dv = make_sdesc(smem_u32(smem + kOffV), kVBytes / 2, 1024, 2);
+    bool ok = true;
+    for (int x = 0; x < 2 && ok; ++x)
+      if (tl[x].mtile * kRows < seqlen_q) ok = mbar_wait(&bars->q_ready[x], 0, a.err, kErrTimeoutQ);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    RouteWalker rw[2];
+#pragma unroll
+    for (int x = 0; x < 2; ++x) rw[x].init(a.mode, tl[x].bits, a.block_n_mask);
+    for (int j = 0; j <= n_iter && ok; ++j) {
+      if (j < n_iter) {
+        const int st = j % kStages;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->full_k[st], (j / kStages) & 1, a.err, kErrTimeoutFull));
+        if (!ok) break;
+        tc_fence_after();
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-          const int nb = tl[x].nb;
-          // PV_X(jj) once P_X(jj) is in TMEM.
-          if (pv_next[x] < s_next[x]) {
-            const int jj = pv_next[x];
-            const int slot = jj & 1;
-            if (mbar_test(&bars->p_ready[x][slot], (jj >> 1) & 1)) {
-              tc_fence_after();
-              const uint32_t vb = smem_u32(smem + kOffV + (jj % kStages) * kVBytes);
+          const int kind = rw[x].kind();
+          rw[x].advance();
+          if (j >= tl[x].nb) continue;
+          const uint32_t d = tbase + col_s(x, j & 1);
+          if (kind == 0) {
+            const uint64_t qa = dq16 + ((x * kQ16Bytes) >> 4);
+            const uint64_t kb = dk16 + ((st * kK16Bytes) >> 4);
 #pragma unroll
-              for (int kk = 0; kk < kKeys / 16; ++kk) {
-                const uint64_t bd = make_sdesc(vb + kk * 16 * 128, kVBytes / 2, 1024, 2);
-                mma_f16_ts(tbase + col_o(x), tbase + col_s(x, slot) + kk * 8, bd, idesc_pv,
-                           (jj > 0 || kk > 0) ? 1u : 0u);
-              }
-              tc_commit(&bars->pv_done[x][slot]);
-              ++pv_next[x];
-              progress = true;
+            for (int kk = 0; kk < kD / 16; ++kk) {
+              const uint32_t off_q = ((kk >> 2) * (kQ16Bytes / 2) + (kk & 3) * 32) >> 4;
+              const uint32_t off_k = ((kk >> 2) * (kK16Bytes / 2) + (kk & 3) * 32) >> 4;
+              mma_f16_ss_e(d, qa + off_q, kb + off_k, idesc_qk16, kk > 0 ? 1u : 0u);
             }
-          }
-          // S_X(j) once K(j) is resident and slot j&1 is free (PV_X(j-2) done).
-          if (s_next[x] < nb) {
-            const int j = s_next[x];
-            const int s = j % kStages;
-            const int slot = j & 1;
-            if (mbar_test(&bars->full[s], (j / kStages) & 1) &&
-                (j < 2 || mbar_test(&bars->pv_done[x][slot], ((j - 2) >> 1) & 1))) {
-              tc_fence_after();
-              const uint32_t d = tbase + col_s(x, slot);
-              if (route_kind(a.mode, tl[x].bits, j, a.block_n_mask) == 0) {
-                const uint32_t qb = smem_u32(smem + kOffQ16 + x * kQ16Bytes);
-                const uint32_t kb = smem_u32(smem + kOffK16 + s * kK16Bytes);
+          } else {
+            const uint64_t qa = dq8 + ((x * kQ8Bytes) >> 4);
+            const uint64_t kb = dk8 + ((st * kK8Bytes) >> 4);
 #pragma unroll
-                for (int kk = 0; kk < kD / 16; ++kk) {
-                  const uint64_t ad = make_sdesc(qb + (kk >> 2) * (kQ16Bytes / 2) + (kk & 3) * 32, 16, 1024, 2);
-                  const uint64_t bd = make_sdesc(kb + (kk >> 2) * (kK16Bytes / 2) + (kk & 3) * 32, 16, 1024, 2);
-                  mma_f16_ss(d, ad, bd, idesc_qk16, kk > 0 ? 1u : 0u);
-                }
-              } else {
-                const uint32_t qb = smem_u32(smem + kOffQ8 + x * kQ8Bytes);
-                const uint32_t kb = smem_u32(smem + kOffK8 + s * kK8Bytes);
-#pragma unroll
-                for (int kk = 0; kk < kD / 32; ++kk) {
-                  const uint64_t ad = make_sdesc(qb + kk * 32, 16, 1024, 2);
-                  const uint64_t bd = make_sdesc(kb + kk * 32, 16, 1024, 2);
-                  mma_i8_ss(d, ad, bd, idesc_qk8, kk > 0 ? 1u : 0u);
-                }
-              }
-              tc_commit(&bars->s_full[x][slot]);
-              ++s_next[x];
-              progress = true;
-            }
+            for (int kk = 0; kk < kD / 32; ++kk) mma_i8_ss_e(d, qa + kk * 2, kb + kk * 2, idesc_qk8, kk > 0 ? 1u : 0u);
           }
-        }
-        // Release a K/V stage once every tile that uses it has issued its PV.
-        while (released < n_iter && (pv_next[0] > released || tl[0].nb <= released) &&
-               (pv_next[1] > released || tl[1].nb <= released)) {
-          tc_commit(&bars->empty[released % kStages]);
-          ++released;
-          progress = true;
-        }
-        if (pv_next[0] >= tl[0].nb && pv_next[1] >= tl[1].nb && released >= n_iter) break;
-        const unsigned long long now = globaltimer_ns();
-        if (progress) {
-          t_last = now;
-        } else if (now - t_last > kWaitTimeoutNs) {
-          record_error(a.err, kErrTimeoutP);
-          ok = false;
+          tc_commit_e(&bars->s_full[x][j & 1]);
         }
       }
-      tc_commit(&bars->mma_done);
-      mbar_wait(&bars->mma_done, 0, a.err, kErrTimeoutDrain);
+      if (j >= 1) {
+        const int jj = j - 1;
+        const int st = jj % kStages;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->full_v[st], (jj / kStages) & 1, a.err, kErrTimeoutFull));
+        if (!ok) break;
+        const uint64_t vb = dv + ((st * kVBytes) >> 4);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          if (jj >= tl[x].nb) continue;
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&bars->p_ready[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutP));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t pa = tbase + col_s(x, jj & 1);
+#pragma unroll
+          for (int kk = 0; kk < kKeys / 16; ++kk)
+            mma_f16_ts_e(tbase + col_o(x), pa + kk * 8, vb + ((kk * 16 * 128) >> 4), idesc_pv,
+                         (jj > 0 || kk > 0) ? 1u : 0u);
+          tc_commit_e(&bars->pv_done[x][jj & 1]);
+        }
+        if (!ok) break;
+        tc_commit_e(&bars->empty[st]);
+      }
     }
+    tc_commit_e(&bars->mma_done);
+    mbar_wait(&bars->mma_done, 0, a.err, kErrTimeoutDrain);
+    __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax warpgroups
     const int x = warp >> 2;
@@ -368,22 +374,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m_used = kNegInf;
       float l = 1.f;
       const int coff = seqlen_k - seqlen_q;
-      // K block scale of tile j, loaded one tile ahead to keep the global load
-      // off the critical path.
-      auto load_sk = [&](int j) -> __half {
-        __half v = __float2half_rn(1.f);
-        if (j < me.nb && ks_end > ks_base && route_kind(a.mode, me.bits, j, a.block_n_mask) == 1) {
-          const int idx = min(ks_base + (j * kKeys) / a.blkk, ks_end - 1);
-          v = a.k_scale[static_cast<int64_t>(idx) * a.HK + hk];
+      // K block scale of a tile, loaded one tile ahead to keep the global load
+      // off the critical path. Routes and scale blocks of consecutive tiles are
+      // tracked incrementally (no per-tile division).
+      RouteWalker rw;
+      rw.init(a.mode, me.bits, a.block_n_mask);
+      const int sk_per = a.blkk / kKeys;  // 64-key tiles per K scale block (blkk % 64 == 0)
+      int sk_idx = ks_base, sk_sub = 0;
+      // The load is unconditional (clamped to a valid row) and its value is only
+      // selected when used, one tile later, so no instruction waits on it early.
+      const bool have_sk = ks_end > ks_base;
+      const __half* sk_col = a.k_scale + hk;
+      auto load_next_sk = [&]() -> __half {  // raw scale of the next tile in order; then step
+        const __half v = have_sk ? sk_col[static_cast<int64_t>(min(sk_idx, ks_end - 1)) * a.HK] : __half();
+        if (++sk_sub == sk_per) {
+          sk_sub = 0;
+          ++sk_idx;
         }
         return v;
       };
-      __half sk_next = load_sk(0);
+      __half sk_next = load_next_sk();
       for (int j = 0; ok && j < me.nb; ++j) {
         const int slot = j & 1;
-        const int kind = route_kind(a.mode, me.bits, j, a.block_n_mask);
-        const __half sk16 = sk_next;
-        sk_next = load_sk(j + 1);
+        const int kind = rw.kind();
+        rw.advance();
+        const __half sk16 = (have_sk && kind == 1) ? sk_next : __float2half_rn(1.f);
+        sk_next = load_next_sk();
         const float ss = kind == 1 ? int8_score_scale(sq16, sk16, a.qk_scale) : 1.f;
         ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[x][slot], (j >> 1) & 1, a.err, kErrTimeoutScores));
         if (!ok) break;
