@@ -19,13 +19,14 @@
 //                     dims), so each producer issues at most two copies per stage:
 //                     a thread's bulk-tensor copies go out one after another, and
 //                     splitting K and V over two warps halves that serial chain.
-//   warp 9            MMA issuer: S_X = Q_X K^T (tcgen05 kind::f16 or kind::i8,
-//                     both operands in shared memory) into a TMEM score slot of
-//                     tile X; O_X += P_X V (kind::f16, P from TMEM, fp32 O).
+//   warps 9 / 11      MMA issuer of tile A / B: S_X = Q_X K^T (tcgen05 kind::f16
+//                     or kind::i8, both operands in shared memory) into a TMEM
+//                     score slot of tile X; O_X += P_X V (kind::f16, P from
+//                     TMEM, fp32 O). Two issuers halve the serial issue chain.
 // TMEM (512 columns): O_A [0,128), O_B [128,256), two 64-column S/P slots per
-// tile at [256,384) and [384,512). Issue order per key tile j:
-//   S_A(j), S_B(j), PV_A(j-1), PV_B(j-1)
-// so that every wait of the MMA thread has other tensor-core work queued.
+// tile at [256,384) and [384,512). Each issuer's order per key tile j is
+//   S_X(j), PV_X(j-1)
+// so S_X(j) runs on the tensor core while the softmax works on tile j-1.
 #include "attn_common.cuh"
 #include "tilemix_b200.h"
 
@@ -39,7 +40,7 @@ constexpr int kStages = 3;
 #define TILEMIX_PAIRED_PREFETCH 0
 #endif
 constexpr int kPrefetch = TILEMIX_PAIRED_PREFETCH;  // key tiles warmed in L2 ahead of the ring (0 = off)
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 
 constexpr uint32_t kQ16Bytes = kRows * kD * 2;  // 32 KB, two 64-column boxes of 16 KB
@@ -58,13 +59,14 @@ constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
 struct Barriers {
   uint64_t full_k[kStages];
   uint64_t full_v[kStages];
-  uint64_t empty[kStages];
+  uint64_t empty_k[kStages];  // K stage free: both tiles' S of that key tile done
+  uint64_t empty_v[kStages];  // V stage free: both tiles' PV of that key tile done
   uint64_t q_full[2];
   uint64_t q_ready[2];
   uint64_t s_full[2][2];
   uint64_t p_ready[2][2];
   uint64_t pv_done[2][2];
-  uint64_t mma_done;
+  uint64_t mma_done[2];
   uint32_t tmem_base;
   float red[2][4];
 };
@@ -125,7 +127,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->full_k[s], 1);
       mbar_init(&bars->full_v[s], 1);
-      mbar_init(&bars->empty[s], 1);
+      mbar_init(&bars->empty_k[s], 2);  // one commit from each MMA warp
+      mbar_init(&bars->empty_v[s], 2);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->q_full[x], 1);
@@ -136,7 +139,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&bars->pv_done[x][s], 1);
       }
     }
-    mbar_init(&bars->mma_done, 1);
+    mbar_init(&bars->mma_done[0], 1);
+    mbar_init(&bars->mma_done[1], 1);
     fence_mbarrier_init();
   }
   if (warp == 9) {
@@ -174,8 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < n_iter && ok; ++j) {
       const int s = j % kStages;
       if (j >= kStages)
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(&bars->empty[s], ((j - kStages) / kStages) & 1, a.err, kErrTimeoutEmpty));
+        ok = __all_sync(0xffffffffu, mbar_wait(is_k ? &bars->empty_k[s] : &bars->empty_v[s],
+                                               ((j - kStages) / kStages) & 1, a.err, kErrTimeoutEmpty));
       if (!ok) break;
       const int tok = k_start + j * kKeys;
       if (is_k) {
@@ -218,89 +222,86 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!is_k)
       for (int x = 0; x < 2; ++x)
         if (tl[x].mtile * kRows < seqlen_q) mbar_wait(&bars->q_full[x], 0, a.err, kErrTimeoutDrain);
-  } else if (warp == 9) {
-    // ------------------------------------------------------------------ MMA issuer
-    // Fixed issue order per key tile j, run by the whole warp with one elected
-    // lane issuing:   S_A(j), S_B(j), PV_A(j-1), PV_B(j-1), release stage j-1.
-    // Every wait is on the input the next group needs, so the tensor core
-    // always has the previous groups queued. S_X(j) overwrites TMEM slot j&1,
-    // which P_X(j-2) occupied: PV_X(j-2) was issued earlier by this thread and
-    // tcgen05.mma operations from one thread execute in issue order, so it has
-    // read P before S_X(j) writes the slot.
+  } else if (warp == 9 || warp == 11) {
+    // ------------------------------------------------------------------ MMA issuers
+    // One warp per query tile X (warp 9: A, warp 11: B, on different SM
+    // sub-partitions), each running converged with one elected lane issuing,
+    // in a fixed order per key tile j:
+    //   S_X(j), release K(j), PV_X(j-1), release V(j-1)
+    // (a stage is free once both warps have committed its release). S_X(j)
+    // overwrites TMEM slot j&1, which P_X(j-2) occupied: PV_X(j-2) was issued
+    // earlier by the same thread and tcgen05.mma operations from one thread
+    // execute in issue order, so it has read P before S_X(j) writes the slot.
     // Descriptors are built once; a byte offset is added as offset >> 4 to the
     // start-address field (all shared-memory offsets here are < 256 KB).
+    const int x = warp == 9 ? 0 : 1;
+    const QTile me = tl[x];
     constexpr uint32_t idesc_qk16 = make_idesc(1, 0, 0, 0, 128, 64);
     constexpr uint32_t idesc_qk8 = make_idesc(2, 1, 0, 0, 128, 64);
     constexpr uint32_t idesc_pv = make_idesc(1, 0, 0, 1, 128, kD);
-    const uint64_t dq16 = make_sdesc(smem_u32(smem + kOffQ16), 16, 1024, 2);
-    const uint64_t dq8 = make_sdesc(smem_u32(smem + kOffQ8), 16, 1024, 2);
+    const uint64_t dq16 = make_sdesc(smem_u32(smem + kOffQ16 + x * kQ16Bytes), 16, 1024, 2);
+    const uint64_t dq8 = make_sdesc(smem_u32(smem + kOffQ8 + x * kQ8Bytes), 16, 1024, 2);
     const uint64_t dk16 = make_sdesc(smem_u32(smem + kOffK16), 16, 1024, 2);
     const uint64_t dk8 = make_sdesc(smem_u32(smem + kOffK8), 16, 1024, 2);
     const uint64_t dv = make_sdesc(smem_u32(smem + kOffV), kVBytes / 2, 1024, 2);
+    const uint32_t d_o = tbase + col_o(x);
     bool ok = true;
-    for (int x = 0; x < 2 && ok; ++x)
-      if (tl[x].mtile * kRows < seqlen_q) ok = mbar_wait(&bars->q_ready[x], 0, a.err, kErrTimeoutQ);
-    ok = __all_sync(0xffffffffu, ok);
+    if (me.mtile * kRows < seqlen_q) ok = __all_sync(0xffffffffu, mbar_wait(&bars->q_ready[x], 0, a.err, kErrTimeoutQ));
     tc_fence_after();
-    RouteWalker rw[2];
-#pragma unroll
-    for (int x = 0; x < 2; ++x) rw[x].init(a.mode, tl[x].bits, a.block_n_mask);
+    RouteWalker rw;
+    rw.init(a.mode, me.bits, a.block_n_mask);
     for (int j = 0; j <= n_iter && ok; ++j) {
       if (j < n_iter) {
         const int st = j % kStages;
+        const int kind = rw.kind();
+        rw.advance();
+        // Wait for K(j) even when this tile does not use it: the release below
+        // must not reach the stage's barrier before the other warp's release of
+        // the previous use of the stage (the copy of K(j) waited for it), or
+        // two releases from this warp could complete one phase.
         ok = __all_sync(0xffffffffu, mbar_wait(&bars->full_k[st], (j / kStages) & 1, a.err, kErrTimeoutFull));
         if (!ok) break;
-        tc_fence_after();
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const int kind = rw[x].kind();
-          rw[x].advance();
-          if (j >= tl[x].nb) continue;
+        if (j < me.nb) {
+          tc_fence_after();
           const uint32_t d = tbase + col_s(x, j & 1);
           if (kind == 0) {
-            const uint64_t qa = dq16 + ((x * kQ16Bytes) >> 4);
             const uint64_t kb = dk16 + ((st * kK16Bytes) >> 4);
 #pragma unroll
             for (int kk = 0; kk < kD / 16; ++kk) {
               const uint32_t off_q = ((kk >> 2) * (kQ16Bytes / 2) + (kk & 3) * 32) >> 4;
               const uint32_t off_k = ((kk >> 2) * (kK16Bytes / 2) + (kk & 3) * 32) >> 4;
-              mma_f16_ss_e(d, qa + off_q, kb + off_k, idesc_qk16, kk > 0 ? 1u : 0u);
+              mma_f16_ss_e(d, dq16 + off_q, kb + off_k, idesc_qk16, kk > 0 ? 1u : 0u);
             }
           } else {
-            const uint64_t qa = dq8 + ((x * kQ8Bytes) >> 4);
             const uint64_t kb = dk8 + ((st * kK8Bytes) >> 4);
 #pragma unroll
-            for (int kk = 0; kk < kD / 32; ++kk) mma_i8_ss_e(d, qa + kk * 2, kb + kk * 2, idesc_qk8, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < kD / 32; ++kk) mma_i8_ss_e(d, dq8 + kk * 2, kb + kk * 2, idesc_qk8, kk > 0 ? 1u : 0u);
           }
           tc_commit_e(&bars->s_full[x][j & 1]);
         }
+        tc_commit_e(&bars->empty_k[st]);  // this warp is done with K(j) once its S has run
       }
       if (j >= 1) {
         const int jj = j - 1;
         const int st = jj % kStages;
         ok = __all_sync(0xffffffffu, mbar_wait(&bars->full_v[st], (jj / kStages) & 1, a.err, kErrTimeoutFull));
         if (!ok) break;
-        const uint64_t vb = dv + ((st * kVBytes) >> 4);
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          if (jj >= tl[x].nb) continue;
-          ok = __all_sync(0xffffffffu,
-                          mbar_wait(&bars->p_ready[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutP));
+        if (jj < me.nb) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->p_ready[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutP));
           if (!ok) break;
           tc_fence_after();
+          const uint64_t vb = dv + ((st * kVBytes) >> 4);
           const uint32_t pa = tbase + col_s(x, jj & 1);
 #pragma unroll
           for (int kk = 0; kk < kKeys / 16; ++kk)
-            mma_f16_ts_e(tbase + col_o(x), pa + kk * 8, vb + ((kk * 16 * 128) >> 4), idesc_pv,
-                         (jj > 0 || kk > 0) ? 1u : 0u);
+            mma_f16_ts_e(d_o, pa + kk * 8, vb + ((kk * 16 * 128) >> 4), idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
           tc_commit_e(&bars->pv_done[x][jj & 1]);
         }
-        if (!ok) break;
-        tc_commit_e(&bars->empty[st]);
+        tc_commit_e(&bars->empty_v[st]);
       }
     }
-    tc_commit_e(&bars->mma_done);
-    mbar_wait(&bars->mma_done, 0, a.err, kErrTimeoutDrain);
+    tc_commit_e(&bars->mma_done[x]);
+    mbar_wait(&bars->mma_done[x], 0, a.err, kErrTimeoutDrain);
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax warpgroups
