@@ -90,10 +90,16 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss,
       h[16 + i] = __floats2half2_rn(__uint_as_float(s1[2 * i]), __uint_as_float(s1[2 * i + 1]));
     }
   } else {
+    // f32(i) * ss in one rounding: with a = float(i + 0x4B400000) = 1.5*2^23 + i,
+    // fma(a, ss, -1.5*2^23*ss) evaluates a*ss - 1.5*2^23*ss = i*ss exactly before
+    // its single rounding (-1.5*2^23*ss is exact: ss has an 11-bit significand).
+    const float c = -12582912.0f * ss;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      h[i] = __floats2half2_rn(i2f_exact(s0[2 * i]) * ss, i2f_exact(s0[2 * i + 1]) * ss);
-      h[16 + i] = __floats2half2_rn(i2f_exact(s1[2 * i]) * ss, i2f_exact(s1[2 * i + 1]) * ss);
+      h[i] = __floats2half2_rn(fmaf(__uint_as_float(s0[2 * i] + 0x4B400000u), ss, c),
+                               fmaf(__uint_as_float(s0[2 * i + 1] + 0x4B400000u), ss, c));
+      h[16 + i] = __floats2half2_rn(fmaf(__uint_as_float(s1[2 * i] + 0x4B400000u), ss, c),
+                                    fmaf(__uint_as_float(s1[2 * i + 1] + 0x4B400000u), ss, c));
     }
   }
   if (lim < kKeys) {

@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t dv = make_sdesc(smem_u32(smem + kOffV), kVBytes / 2, 1024, 2);
     const uint32_t d_o = tbase + col_o(x);
     bool ok = true;
-    if (me.mtile * kRows < seqlen_q) ok = __all_sync(0xffffffffu, mbar_wait(&bars->q_ready[x], 0, a.err, kErrTimeoutQ));
+    if (me.mtile * kRows < seqlen_q) ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_ready[x], 0, a.err, kErrTimeoutQ));
     tc_fence_after();
     RouteWalker rw;
     rw.init(a.mode, me.bits, a.block_n_mask);
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // must not reach the stage's barrier before the other warp's release of
         // the previous use of the stage (the copy of K(j) waited for it), or
         // two releases from this warp could complete one phase.
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->full_k[st], (j / kStages) & 1, a.err, kErrTimeoutFull));
+        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->full_k[st], (j / kStages) & 1, a.err, kErrTimeoutFull));
         if (!ok) break;
         if (j < me.nb) {
           tc_fence_after();
@@ -284,10 +284,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j >= 1) {
         const int jj = j - 1;
         const int st = jj % kStages;
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->full_v[st], (jj / kStages) & 1, a.err, kErrTimeoutFull));
+        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->full_v[st], (jj / kStages) & 1, a.err, kErrTimeoutFull));
         if (!ok) break;
         if (jj < me.nb) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&bars->p_ready[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutP));
+          ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->p_ready[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutP));
           if (!ok) break;
           tc_fence_after();
           const uint64_t vb = dv + ((st * kVBytes) >> 4);
@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const __half sk16 = (have_sk && kind == 1) ? sk_next : __float2half_rn(1.f);
         sk_next = load_next_sk();
         const float ss = kind == 1 ? int8_score_scale(sq16, sk16, a.qk_scale) : 1.f;
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[x][slot], (j >> 1) & 1, a.err, kErrTimeoutScores));
+        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->s_full[x][slot], (j >> 1) & 1, a.err, kErrTimeoutScores));
         if (!ok) break;
         tc_fence_after();
         int lim = seqlen_k - j * kKeys;
@@ -415,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (__any_sync(0xffffffffu, need_rescale)) {
           const int jj = j - 1;
           ok = __all_sync(0xffffffffu,
-                          mbar_wait(&bars->pv_done[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutPV));
+                          mbar_wait_spin(&bars->pv_done[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutPV));
           if (!ok) break;
           tc_fence_after();
           rescale_o_row<kD>(tbase + lane_off + col_o(x), o_scale);

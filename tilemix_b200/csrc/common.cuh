@@ -92,13 +92,44 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware keep the thread suspended for up to
+// `suspend_ns` while the phase is incomplete (it resumes as soon as the phase
+// completes), so a waiting warp takes no issue slots from the others.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete; false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      record_error(err, code);
+      return false;
+    }
+  }
+}
+
+// Polling wait for waits on the critical path: a thread suspended inside
+// try_wait resumes on the order of a thousand cycles after the phase
+// completes, while a test_wait loop sees it within a few tens of cycles (at
+// the price of issue slots). Bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_test(bar, parity)) return true;
+    if ((n & 1023u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
       record_error(err, code);
       return false;
     }
