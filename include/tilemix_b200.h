@@ -177,6 +177,23 @@ typedef struct tm_attn_tuning {
 /* tm_attn_fwd with explicit tuning (NULL = defaults of tm_attn_fwd). */
 int tm_attn_fwd_ex(const tm_attn_params* params, const tm_attn_tuning* tuning, void* stream);
 
+/*
+ * tm_attn_fwd_ex for callers that cannot allocate device memory (no
+ * counterpart in the reference): a host whose framework owns every device
+ * allocation and hands the library only Q/K/V/O, or a plugin hook in which
+ * allocating is not allowed, can still run the INT8 routes. The quantised K
+ * operand that tm_attn_fwd takes from caller buffers is produced inside this
+ * call into fixed-size scratch reserved by the library (16 MiB of K codes:
+ * k_tokens * heads_k * head_dim <= 16,777,216; (k_tokens / blkk + batch) *
+ * heads_k <= 262,144 scales; batch <= 65,535); larger problems return
+ * TM_ERR_UNSUPPORTED. params->k8, k_scale and cu_k_scale must be NULL. The
+ * call allocates nothing. The first call on a device resolves the scratch
+ * address (a runtime query), so make it before capturing a stream. Calls that
+ * may overlap on the GPU (several streams or threads) share the scratch and
+ * must be serialised by the caller.
+ */
+int tm_attn_fwd_noalloc(const tm_attn_params* params, const tm_attn_tuning* tuning, void* stream);
+
 /* Human-readable text for a TM_* status code. */
 const char* tm_status_string(int status);
 

@@ -74,6 +74,7 @@ SIGNATURES = {
                                         c_void_p]),
     "tm_attn_fwd": (c_int, [ctypes.POINTER(TmAttnParams), c_void_p]),
     "tm_attn_fwd_ex": (c_int, [ctypes.POINTER(TmAttnParams), ctypes.POINTER(TmAttnTuning), c_void_p]),
+    "tm_attn_fwd_noalloc": (c_int, [ctypes.POINTER(TmAttnParams), ctypes.POINTER(TmAttnTuning), c_void_p]),
     "tm_build_precision_map": (c_int, [ctypes.POINTER(TmMapParams), c_void_p, c_void_p, c_void_p]),
     "tm_status_string": (ctypes.c_char_p, [c_int]),
 }

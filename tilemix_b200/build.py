@@ -21,7 +21,7 @@ LIB_NAME = "libtilemix_b200.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
 SOURCES = ["attn_api.cu", "attn_fwd_general.cu", "attn_fwd_paired.cu", "attn_fwd_persistent.cu", "quant.cu",
-           "precision_map.cu"]
+           "precision_map.cu", "attn_noalloc.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
