@@ -170,7 +170,9 @@ typedef struct tm_attn_tuning {
   /* Kernel selection: 0 = automatic (the paired kernel when head_dim is 128,
    * block_m 128 and Q is quantised in kernel, else the general kernel);
    * 1 = always the general kernel; 2 = the persistent route-compacted kernel
-   * where the paired one would apply. */
+   * where the paired one would apply; 3 = the paired kernel with 128-key
+   * softmax steps there; 4 = the paired kernel with each score row split
+   * across two softmax warps there. */
   int force_general;
 } tm_attn_tuning;
 

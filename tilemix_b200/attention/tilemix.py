@@ -201,7 +201,7 @@ def _launch(q, k, v, o, cu_q, cu_k, bitmask, max_q, max_k, *, q8=None, sq=None, 
     p.sched_workspace = _ptr(_sched_word(q.device))
     tune = TmAttnTuning()
     tune.rescale_threshold = rescale_threshold() if threshold is None else float(threshold)
-    tune.force_general = {"general": 1, "persistent": 2}.get(
+    tune.force_general = {"general": 1, "persistent": 2, "paired128": 3, "split": 4}.get(
         os.environ.get("TILEMIX_B200_KERNEL", "").strip().lower(), 0)
     stream = torch.cuda.current_stream(q.device).cuda_stream
     with torch.cuda.device(q.device):

@@ -2,6 +2,10 @@
 // dispatch between the two sm_100a kernels:
 //   * paired  (attn_fwd_paired.cu): head_dim 128, block_m 128, Q quantised in
 //     kernel (or FP16-only routing) -- the model / tilemix_attention_with_quant path;
+//   * paired128 (attn_fwd_paired128.cu): the same shapes with 128-key softmax
+//     steps and one score slot per tile; selected explicitly (force_general == 3);
+//   * split (attn_fwd_split.cu): the same shapes with every score row shared by
+//     two softmax warps (16 softmax warps); selected explicitly (force_general == 4);
 //   * persistent (attn_fwd_persistent.cu): same shapes, route-compacted
 //     persistent schedule; selected explicitly (tuning.force_general == 2);
 //   * general (attn_fwd_general.cu): everything else the API accepts (block_m 64,
@@ -21,6 +25,10 @@ int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUten
                        const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
 int launch_attn_persistent(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
                            const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
+int launch_attn_paired128(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
+                          const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
+int launch_attn_split(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
+                      const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -79,7 +87,7 @@ extern "C" int tm_attn_fwd(const tm_attn_params* p, void* stream) { return tm_at
 
 extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tuning, void* stream) {
   const float rescale_threshold = tuning ? tuning->rescale_threshold : 0.f;
-  const int kernel_choice = tuning ? tuning->force_general : 0;  // 0 auto, 1 general, 2 persistent
+  const int kernel_choice = tuning ? tuning->force_general : 0;  // 0 auto, 1 general, 2 persistent, 3 paired128, 4 split
   const int force_general = kernel_choice == 1;
   using namespace tilemix;
   if (p == nullptr) return TM_ERR_NULL;
@@ -187,6 +195,8 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
     if (rc != TM_OK) return rc;
     rc = make_map_d128(&v4, p->v, p->heads_k, p->k_tokens, p->v_stride_head, p->v_stride_tok, 64);
     if (rc != TM_OK) return rc;
+    if (kernel_choice == 3) return launch_attn_paired128(q4, k4, m_k8, v4, a, p->batch, p->max_seqlen_q, st);
+    if (kernel_choice == 4) return launch_attn_split(q4, k4, m_k8, v4, a, p->batch, p->max_seqlen_q, st);
     return launch_attn_paired(q4, k4, m_k8, v4, a, p->batch, p->max_seqlen_q, st);
   }
   const int tiles = (p->max_seqlen_q + 127) / 128;

@@ -297,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           named_bar_sync_softmax();
           m = fmaxf(fmaxf(bars->red[0], bars->red[1]), fmaxf(bars->red[2], bars->red[3]));
           const float scale = __fdiv_rn(m, 127.f);
+          const float rscale = __frcp_rn(scale);
           sq16 = __float2half_rn(scale);
 #pragma unroll
           for (int c8 = 0; c8 < D / 8; ++c8) {
@@ -305,8 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 f = __half22float2(h[e]);
-              const uint32_t pr = (static_cast<uint32_t>(quant_code(f.x, scale)) & 0xFFu) |
-                                  ((static_cast<uint32_t>(quant_code(f.y, scale)) & 0xFFu) << 8);
+              const uint32_t pr = (static_cast<uint32_t>(quant_code_rcp(f.x, scale, rscale)) & 0xFFu) |
+                                  ((static_cast<uint32_t>(quant_code_rcp(f.y, scale, rscale)) & 0xFFu) << 8);
               if (e < 2)
                 w0 |= pr << (16 * e);
               else

@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < n_iter && ok; ++j) {
       const int s = j % kStages;
       if (j >= kStages)
-        ok = __all_sync(0xffffffffu, mbar_wait(is_k ? &bars->empty_k[s] : &bars->empty_v[s],
+        ok = __all_sync(0xffffffffu, mbar_wait_spin(is_k ? &bars->empty_k[s] : &bars->empty_v[s],
                                                ((j - kStages) / kStages) & 1, a.err, kErrTimeoutEmpty));
       if (!ok) break;
       const int tok = k_start + j * kKeys;
@@ -313,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tile_ok) {
       const int row = me.mtile * kRows + t;
       const bool row_ok = row < seqlen_q;
-      bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->q_full[x], 0, a.err, kErrTimeoutQ));
+      bool ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_full[x], 0, a.err, kErrTimeoutQ));
       __half sq16 = __float2half_rn(1.f);
       {
         // Scale Q in place (elementwise, so the swizzled layout is irrelevant)
@@ -343,6 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           asm volatile("bar.sync %0, 128;" ::"r"(1 + x) : "memory");
           m = fmaxf(fmaxf(bars->red[x][0], bars->red[x][1]), fmaxf(bars->red[x][2], bars->red[x][3]));
           const float scale = __fdiv_rn(m, 127.f);
+          const float rscale = __frcp_rn(scale);
           sq16 = __float2half_rn(scale);
           uint8_t* q8 = smem + kOffQ8 + x * kQ8Bytes;
 #pragma unroll
@@ -356,10 +357,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int e = 0; e < 2; ++e) {
                 const float2 f0 = __half22float2(h[2 * e]);
                 const float2 f1 = __half22float2(h[2 * e + 1]);
-                w[hc * 2 + e] = (static_cast<uint32_t>(quant_code(f0.x, scale)) & 0xFFu) |
-                                ((static_cast<uint32_t>(quant_code(f0.y, scale)) & 0xFFu) << 8) |
-                                ((static_cast<uint32_t>(quant_code(f1.x, scale)) & 0xFFu) << 16) |
-                                ((static_cast<uint32_t>(quant_code(f1.y, scale)) & 0xFFu) << 24);
+                w[hc * 2 + e] = (static_cast<uint32_t>(quant_code_rcp(f0.x, scale, rscale)) & 0xFFu) |
+                                ((static_cast<uint32_t>(quant_code_rcp(f0.y, scale, rscale)) & 0xFFu) << 8) |
+                                ((static_cast<uint32_t>(quant_code_rcp(f1.x, scale, rscale)) & 0xFFu) << 16) |
+                                ((static_cast<uint32_t>(quant_code_rcp(f1.y, scale, rscale)) & 0xFFu) << 24);
               }
             }
             *reinterpret_cast<uint4*>(q8 + t * 128 + ((g ^ (t & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -428,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __half* orow = a.out + (static_cast<int64_t>(q_start) + row) * a.o_st + static_cast<int64_t>(me.hq) * a.o_sh;
       if (ok && me.nb > 0) {
         const int jj = me.nb - 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutPV));
+        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->pv_done[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutPV));
         tc_fence_after();
       }
       store_o_row<kD>(tbase + lane_off + col_o(x), me.nb > 0, l, orow, row_ok && ok);

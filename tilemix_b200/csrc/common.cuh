@@ -29,6 +29,7 @@ enum : int {
   kErrTimeoutPV = 5,        // waited too long for a PV completion
   kErrTimeoutQ = 6,         // MMA warp waited too long for Q in TMEM
   kErrTimeoutDrain = 7,     // final drain of in-flight work timed out
+  kErrTimeoutExchange = 8,  // partner thread of a split softmax row never published its value
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
@@ -415,6 +416,18 @@ __device__ __forceinline__ uint32_t pack_half2_rn(float lo, float hi) {
 // truncate toward zero (NaN -> 0).
 __device__ __forceinline__ int quant_code(float x, float scale) {
   float y = __fdiv_rn(x, scale);
+  y = __fadd_rn(y, y >= 0.f ? 0.5f : -0.5f);
+  return __float2int_rz(y);
+}
+
+// quant_code with the quotient formed from the block's correctly rounded
+// reciprocal rcp = 1/scale and one FMA residual correction (Markstein):
+// q0 = x*rcp, q = q0 + (x - q0*scale)*rcp. For every finite fp16 x and every
+// scale = fp16 magnitude / 127 this equals the IEEE quotient x / scale (checked
+// exhaustively on a B200), except that x = -0 gives +0, which yields the same code.
+__device__ __forceinline__ int quant_code_rcp(float x, float scale, float rcp) {
+  const float q0 = x * rcp;
+  float y = fmaf(fmaf(-q0, scale, x), rcp, q0);
   y = __fadd_rn(y, y >= 0.f ? 0.5f : -0.5f);
   return __float2int_rz(y);
 }
