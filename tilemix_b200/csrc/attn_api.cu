@@ -148,6 +148,7 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   a.out = static_cast<__half*>(p->out);
   a.o_st = p->o_stride_tok;
   a.o_sh = p->o_stride_head;
+  a.o_vec32 = (reinterpret_cast<uintptr_t>(p->out) % 32 == 0 && p->o_stride_tok % 16 == 0 && p->o_stride_head % 16 == 0) ? 1 : 0;
   a.q8 = p->q8;
   a.q8_st = p->q8_stride_tok;
   a.q8_sh = p->q8_stride_head;

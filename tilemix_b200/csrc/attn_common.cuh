@@ -39,6 +39,7 @@ struct AttnArgs {
   int block_m, block_n_mask, blkq, blkk;
   int causal, mode, fuse_q;
   int pair_heads;  // paired kernel: 1 = CTA holds two heads of one KV group, 0 = two m-tiles of one head
+  int o_vec32;     // O rows start on 32-byte boundaries (out 32-byte aligned, strides multiples of 16)
   float qk_scale;
   float rescale_threshold;
   int* err;
@@ -67,6 +68,69 @@ __device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
   return r;
 }
 
+__device__ __forceinline__ uint64_t f32x2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f32x2_add_rm(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// f32(lo or hi half of an fp16 pair) + c, one rounding, on the FMA pipe.
+__device__ __forceinline__ float add_f32_f16_lo(uint32_t h2, float c) {
+  float r;
+  asm("{.reg .f16 l, h;\n\tmov.b32 {l, h}, %1;\n\tadd.rn.f32.f16 %0, l, %2;\n\t}" : "=f"(r) : "r"(h2), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float add_f32_f16_hi(uint32_t h2, float c) {
+  float r;
+  asm("{.reg .f16 l, h;\n\tmov.b32 {l, h}, %1;\n\tadd.rn.f32.f16 %0, h, %2;\n\t}" : "=f"(r) : "r"(h2), "f"(c));
+  return r;
+}
+__device__ __forceinline__ uint32_t hmax2_u32(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// 2^x for a pair of x in [-126, 16) without the MUFU pipe: x = j + f with
+// j = floor(x) (an add rounded toward -inf against 1.5 * 2^23 leaves j in the
+// low mantissa bits), 2^f on [0, 1) by a degree-5 polynomial in Horner form
+// (relative-error minimax fit by the Remez exchange: max relative error
+// 1.5e-7 evaluated in fp32, the accuracy class of ex2.approx), and 2^j added to
+// the exponent field as an integer. Spreads part of the softmax exponentials
+// over the FMA pipe: the MUFU pipe (16 results per clock per SM) is the
+// softmax's throughput limit otherwise.
+__device__ __forceinline__ void exp2_poly_x2(float x0, float x1, float& e0, float& e1) {
+  const uint64_t kMagic = 0x4B4000004B400000ull;  // (1.5 * 2^23, 1.5 * 2^23)
+  const uint64_t x = f32x2_pack(x0, x1);
+  const uint64_t t = f32x2_add_rm(x, kMagic);    // 1.5 * 2^23 + floor(x), exact
+  const uint64_t f = f32x2_add(x, f32x2_sub(kMagic, t));  // x - floor(x) in [0, 1), exact
+  uint64_t p = f32x2_fma(0x3AF619053AF61905ull, f, 0x3C1348063C134806ull);
+  p = f32x2_fma(p, f, 0x3D64AA233D64AA23ull);
+  p = f32x2_fma(p, f, 0x3E75EAD43E75EAD4ull);
+  p = f32x2_fma(p, f, 0x3F31727B3F31727Bull);
+  p = f32x2_fma(p, f, 0x3F7FFFFF3F7FFFFFull);
+  // (1.5 * 2^23 + j) << 23 == j << 23 modulo 2^32.
+  e0 = __uint_as_float(static_cast<uint32_t>(p) + (static_cast<uint32_t>(t) << 23));
+  e1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(t >> 32) << 23));
+}
+
+// Pairs of a 64-key tile whose exponentials run on the FMA pipe (8 of 32).
+__device__ __forceinline__ constexpr bool exp_on_fma(int pair) { return (pair & 3) == 3; }
+
 // One softmax step over a 64-key tile for this thread's row.
 //   taddr     TMEM address (lane and first column) of the 64 score columns
 //   kind      0: fp32 scores (FP16 route)   1: int32 scores (INT8 route)
@@ -75,52 +139,48 @@ __device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
 //   thr       rescale threshold (0 = reference rule)
 // Outputs the packed fp16 P row in p[32]; o_scale/need_rescale say whether the
 // O accumulator row has to be multiplied by o_scale before this P is added.
+// The row maximum is taken over the fp32 values before their fp16 rounding:
+// rounding to nearest is monotonic, so fp16(max v) = max fp16(v).
 __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss, int lim, float thr,
                                              float& m_used, float& l, uint32_t (&p)[32], float& o_scale,
                                              bool& need_rescale) {
-  uint32_t s0[32], s1[32];
-  tmem_ld32(taddr, s0);
-  tmem_ld32(taddr + 32, s1);
+  uint32_t s[64];
+  tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+  tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
   tmem_wait_ld();
-  __half2 h[32];
-  if (kind == 0) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      h[i] = __floats2half2_rn(__uint_as_float(s0[2 * i]), __uint_as_float(s0[2 * i + 1]));
-      h[16 + i] = __floats2half2_rn(__uint_as_float(s1[2 * i]), __uint_as_float(s1[2 * i + 1]));
-    }
-  } else {
+  if (kind != 0) {
     // f32(i) * ss in one rounding: with a = float(i + 0x4B400000) = 1.5*2^23 + i,
     // fma(a, ss, -1.5*2^23*ss) evaluates a*ss - 1.5*2^23*ss = i*ss exactly before
     // its single rounding (-1.5*2^23*ss is exact: ss has an 11-bit significand).
     const float c = -12582912.0f * ss;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      h[i] = __floats2half2_rn(fmaf(__uint_as_float(s0[2 * i] + 0x4B400000u), ss, c),
-                               fmaf(__uint_as_float(s0[2 * i + 1] + 0x4B400000u), ss, c));
-      h[16 + i] = __floats2half2_rn(fmaf(__uint_as_float(s1[2 * i] + 0x4B400000u), ss, c),
-                                    fmaf(__uint_as_float(s1[2 * i + 1] + 0x4B400000u), ss, c));
-    }
-  }
-  if (lim < kKeys) {
-    const __half ninf = __ushort_as_half(0xFC00);
+    const uint64_t ss2 = f32x2_pack(ss, ss), c2 = f32x2_pack(c, c);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const __half lo = (2 * i < lim) ? __low2half(h[i]) : ninf;
-      const __half hi = (2 * i + 1 < lim) ? __high2half(h[i]) : ninf;
-      h[i] = __halves2half2(lo, hi);
+      const uint64_t a2 = f32x2_pack(__uint_as_float(s[2 * i] + 0x4B400000u), __uint_as_float(s[2 * i + 1] + 0x4B400000u));
+      const float2 v = f32x2_unpack(f32x2_fma(a2, ss2, c2));
+      s[2 * i] = __float_as_uint(v.x);
+      s[2 * i + 1] = __float_as_uint(v.y);
     }
   }
-  __half2 mt[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) mt[i] = __hmax2(h[i], h[16 + i]);
-#pragma unroll
-  for (int w = 8; w >= 1; w >>= 1) {
-#pragma unroll
-    for (int i = 0; i < w; ++i) mt[i] = __hmax2(mt[i], mt[i + w]);
-  }
   const float kNegInf = -__int_as_float(0x7f800000);
-  const float mx = fmaxf(__low2float(mt[0]), __high2float(mt[0]));
+  if (__any_sync(0xffffffffu, lim < kKeys)) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i)
+      if (i >= lim) s[i] = 0xFF800000u;  // -inf
+  }
+  // Row maximum: a tree of 3-input maxima (64 -> 22 -> 8 -> 4 -> 2 -> 1).
+  float m1[22];
+#pragma unroll
+  for (int i = 0; i < 21; ++i)
+    m1[i] = max3f(__uint_as_float(s[3 * i]), __uint_as_float(s[3 * i + 1]), __uint_as_float(s[3 * i + 2]));
+  m1[21] = __uint_as_float(s[63]);
+  float m2[8];
+#pragma unroll
+  for (int i = 0; i < 7; ++i) m2[i] = max3f(m1[3 * i], m1[3 * i + 1], m1[3 * i + 2]);
+  m2[7] = m1[21];
+  const float m3a = max3f(m2[0], m2[1], m2[2]), m3b = max3f(m2[3], m2[4], m2[5]);
+  const float mraw = max3f(m3a, m3b, fmaxf(m2[6], m2[7]));
+  const float mx = __half2float(__float2half_rn(mraw));
   const bool has = mx != kNegInf;
   o_scale = 1.f;
   need_rescale = false;
@@ -134,19 +194,34 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss,
   if (has) {
     // l accumulates the exponentials before their fp16 rounding (two packed
     // partial sums); the rounding of p stays exactly the reference's.
-    const uint64_t negm = f32x2_pack(-m_used, -m_used);
+    const float negm = -m_used;
+    // Lower clamp for the FMA-pipe pairs: x >= floor16(m_used - 120) - m_used
+    // keeps floor(x) >= -126; every clamped weight is below 2^-120, which is 0
+    // in fp16 and below the resolution of l.
+    uint32_t lo2;
+    {
+      const float lo = fmaxf(m_used - 120.f, -65504.f);
+      uint16_t lh;
+      asm("cvt.rp.f16.f32 %0, %1;" : "=h"(lh) : "f"(lo));
+      lo2 = static_cast<uint32_t>(lh) * 0x10001u;
+    }
     uint64_t acc0 = 0, acc1 = 0;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const float2 f = __half22float2(h[i]);
-      const float2 d = f32x2_unpack(f32x2_add(f32x2_pack(f.x, f.y), negm));
-      const float e0 = ex2_approx(d.x), e1 = ex2_approx(d.y);
-      const __half2 ph = __floats2half2_rn(e0, e1);
+      uint32_t h2 = pack_half2_rn(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]));
+      float e0, e1;
+      if (exp_on_fma(i)) {
+        h2 = hmax2_u32(h2, lo2);
+        exp2_poly_x2(add_f32_f16_lo(h2, negm), add_f32_f16_hi(h2, negm), e0, e1);
+      } else {
+        e0 = ex2_approx(add_f32_f16_lo(h2, negm));
+        e1 = ex2_approx(add_f32_f16_hi(h2, negm));
+      }
       if (i & 1)
         acc1 = f32x2_add(acc1, f32x2_pack(e0, e1));
       else
         acc0 = f32x2_add(acc0, f32x2_pack(e0, e1));
-      p[i] = *reinterpret_cast<const uint32_t*>(&ph);
+      p[i] = pack_half2_rn(e0, e1);
     }
     const float2 a0 = f32x2_unpack(acc0), a1 = f32x2_unpack(acc1);
     l += (a0.x + a0.y) + (a1.x + a1.y);

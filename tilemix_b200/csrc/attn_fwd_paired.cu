@@ -3,13 +3,27 @@
 // what the model integration and tilemix_attention_with_quant use.
 //
 // Same semantics as the general kernel (attention/triton/tilemix.py:503-951);
-// different mapping. One CTA owns two 128-row query tiles X = A, B that share a
-// KV head: either two Q heads of one GQA group at the same query block (their
+// different mapping. A work item is two 128-row query tiles X = A, B that share
+// a KV head: either two Q heads of one GQA group at the same query block (their
 // routing words are the same map row), or two consecutive query blocks of one
 // head. Every K/V tile is loaded once into shared memory and feeds both tiles.
 //
+// Persistent: one CTA per SM walks a static list of work items, longest first
+// (the last query blocks under causal masking), dealt out in snake order
+// (round r gives CTA c item r*G + c, or r*G + G-1-c for odd r). Barrier phases
+// run on across items, and the item boundary is overlapped:
+//   * the Q producer refills a tile's Q buffers once that tile's own last S
+//     MMA of the current item has completed (q_empty), from L2 (it prefetches
+//     the next item's Q tiles into L2 when an item starts). Issuing the copy
+//     earlier (from the MMA warp right after that S) measured slower: the
+//     transform then overlaps the other tile's last softmax steps;
+//   * the softmax warpgroup transforms the next item's Q (scale, quantise)
+//     while the last PV of the current item runs, then writes the current
+//     item's O; meanwhile the MMA warp already runs the next item's first two
+//     S tiles. Its first PV waits for o_free (the previous O read out of TMEM).
+//
 //   warps 0-3 / 4-7   softmax warpgroup of tile A / B (thread = query row =
-//                     TMEM lane). At start: scale Q in place in shared memory
+//                     TMEM lane). Per item: scale Q in place in shared memory
 //                     (fp16(q * sm_scale * log2e)) and quantise it per 128-row
 //                     block into the INT8 operand (BLKQ = 128 block = the tile).
 //   warp 8            TMA producer of K (only the formats routed by either tile),
@@ -36,10 +50,6 @@ namespace paired {
 constexpr int kD = 128;
 constexpr int kRows = 128;
 constexpr int kStages = 3;
-#ifndef TILEMIX_PAIRED_PREFETCH
-#define TILEMIX_PAIRED_PREFETCH 0
-#endif
-constexpr int kPrefetch = TILEMIX_PAIRED_PREFETCH;  // key tiles warmed in L2 ahead of the ring (0 = off)
 constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 
@@ -61,8 +71,10 @@ struct Barriers {
   uint64_t full_v[kStages];
   uint64_t empty_k[kStages];  // K stage free: both tiles' S of that key tile done
   uint64_t empty_v[kStages];  // V stage free: both tiles' PV of that key tile done
-  uint64_t q_full[2];
-  uint64_t q_ready[2];
+  uint64_t q_full[2];         // per item: Q tile landed (or a plain arrive when the tile is absent)
+  uint64_t q_ready[2];        // per item: Q transformed by the softmax warpgroup (128 arrivals)
+  uint64_t q_empty[2];        // per item: every S of the tile completed, its Q buffers may be refilled
+  uint64_t o_free[2];         // per item: O of the tile read out of TMEM (128 arrivals)
   uint64_t s_full[2][2];
   uint64_t p_ready[2][2];
   uint64_t pv_done[2][2];
@@ -70,6 +82,7 @@ struct Barriers {
   uint32_t tmem_base;
   float red[2][4];
 };
+static_assert(sizeof(Barriers) <= 512, "barrier block");
 
 struct QTile {
   uint64_t bits;
@@ -78,50 +91,244 @@ struct QTile {
   int nb;  // 64-key tiles visited (0 = tile absent)
 };
 
+// One work item, resolved from its index. Items are ordered by level x (0 =
+// the last query block pair, the longest under causal masking), then sequence,
+// then head slot.
+struct Item {
+  QTile tl[2];
+  int q_start, seqlen_q, k_start, seqlen_k;
+  int ks_base, ks_end;  // K scale-block rows of the sequence (INT8 routes)
+  int b, hk, n_iter;
+};
+
+struct Grid {
+  int nx, ny, nz, n_items;
+};
+
+__device__ __forceinline__ Item load_item(int it, const AttnArgs& a, const Grid& g) {
+  Item m;
+  const int per_level = g.ny * g.nz;
+  const int x = it / per_level;
+  const int rem = it - x * per_level;
+  const int z = rem / g.ny;
+  const int y = rem - z * g.ny;
+  m.b = z;
+  m.q_start = a.cu_q[z];
+  m.seqlen_q = a.cu_q[z + 1] - m.q_start;
+  m.k_start = a.cu_k[z];
+  m.seqlen_k = a.cu_k[z + 1] - m.k_start;
+  m.ks_base = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[z] : 0;
+  m.ks_end = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[z + 1] : 0;
+  const int m_blocks = (m.seqlen_q + kRows - 1) / kRows;
+  const int rev = g.nx - 1 - x;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    if (a.pair_heads) {
+      m.tl[t].hq = 2 * y + t;
+      m.tl[t].mtile = rev;
+    } else {
+      m.tl[t].hq = y;
+      m.tl[t].mtile = 2 * rev + t;
+    }
+    const bool valid = m.tl[t].mtile * kRows < m.seqlen_q;
+    m.tl[t].nb = valid ? visited_key_tiles(m.tl[t].mtile * kRows, kRows, m.seqlen_q, m.seqlen_k, a.causal) : 0;
+    m.tl[t].bits = 0;
+    if (valid && a.mode == TM_ROUTE_MIXED)
+      m.tl[t].bits = a.bitmask[static_cast<int64_t>(m.tl[t].hq / a.group) * m_blocks + m.tl[t].mtile];
+  }
+  m.hk = m.tl[0].hq / a.group;  // both tiles share the KV head
+  m.n_iter = max(m.tl[0].nb, m.tl[1].nb);
+  return m;
+}
+
+// Item of round r for this CTA (snake order), or -1 past the end.
+__device__ __forceinline__ int item_index(int r, const Grid& g) {
+  const int G = static_cast<int>(gridDim.x);
+  const int c = static_cast<int>(blockIdx.x);
+  const int it = r * G + ((r & 1) ? G - 1 - c : c);
+  return it < g.n_items ? it : -1;
+}
+
+// Walks this CTA's items, skipping those without any query row (possible with
+// varlen batches). Every role runs the same walk, so all agree on the items.
+struct ItemWalk {
+  int r = 0;
+  __device__ __forceinline__ int next(const AttnArgs& a, const Grid& g, Item& m) {
+    for (;;) {
+      const int it = item_index(r++, g);
+      if (it < 0) return -1;
+      m = load_item(it, a, g);
+      if (m.tl[0].nb > 0 || m.tl[1].nb > 0) return it;
+      // an item whose tiles are both present has nb > 0; both absent: skip
+      if (m.tl[0].mtile * kRows < m.seqlen_q || m.tl[1].mtile * kRows < m.seqlen_q) return it;
+    }
+  }
+};
+
+// Tile x of an item, selected by value (x is a runtime value: indexing the
+// array would place the item in local memory).
+__device__ __forceinline__ QTile tile_of(const Item& m, int x) {
+  QTile q;
+  q.bits = x ? m.tl[1].bits : m.tl[0].bits;
+  q.hq = x ? m.tl[1].hq : m.tl[0].hq;
+  q.mtile = x ? m.tl[1].mtile : m.tl[0].mtile;
+  q.nb = x ? m.tl[1].nb : m.tl[0].nb;
+  return q;
+}
+
+__device__ __forceinline__ bool tile_valid(const Item& m, int x) { return tile_of(m, x).mtile * kRows < m.seqlen_q; }
+
 __device__ __forceinline__ uint32_t col_o(int x) { return static_cast<uint32_t>(x) * 128u; }
 __device__ __forceinline__ uint32_t col_s(int x, int slot) {
   return 256u + static_cast<uint32_t>(x) * 128u + static_cast<uint32_t>(slot) * 64u;
 }
 
+// Scale this thread's Q row in place and build its row of the INT8 operand;
+// the block scale is the maximum over the 128 rows (named barrier 1 + x over
+// the tile's 128 threads). Two passes over shared memory (absmax, then codes
+// and scaling) keep a few registers live instead of the whole row, and the
+// codes come from FMA-pipe arithmetic (quant_code_pair_fma), which leaves the
+// conversion pipe to the other tile's softmax exponentials. Returns the fp16
+// block scale.
+__device__ __forceinline__ __half transform_q(uint8_t* smem, Barriers* bars, const AttnArgs& a, int x, int t,
+                                              int warp, int lane, bool row_ok) {
+  uint8_t* q16 = smem + kOffQ16 + x * kQ16Bytes;
+  // 16-byte chunk c (dims 8c .. 8c+7) of this row in the 128-byte-swizzled tile
+  auto chunk = [&](int c) {
+    return reinterpret_cast<uint4*>(q16 + (c >> 3) * (kQ16Bytes / 2) + t * 128 + (((c & 7) ^ (t & 7)) << 4));
+  };
+  const uint64_t qk2 = f32x2_pack(a.qk_scale, a.qk_scale);
+  auto scale_pair = [&](uint32_t h2) {  // fp16(x * qk_scale) of a pair
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f32x2_pack(f.x, f.y)), "l"(qk2));
+    const float2 v = f32x2_unpack(r);
+    return pack_half2_rn(v.x, v.y);
+  };
+  if (a.mode == TM_ROUTE_FP16) {
+#pragma unroll 4
+    for (int c = 0; c < 16; ++c) {
+      const uint4 r = *chunk(c);
+      *chunk(c) = make_uint4(scale_pair(r.x), scale_pair(r.y), scale_pair(r.z), scale_pair(r.w));
+    }
+    fence_proxy_async_smem();
+    return __float2half_rn(1.f);
+  }
+  // Pass 1: absmax of the row on fp16 pairs (|x| by clearing the sign bits).
+  uint32_t am2 = 0u;
+  if (row_ok) {
+#pragma unroll 4
+    for (int c = 0; c < 16; ++c) {
+      const uint4 r = *chunk(c);
+      am2 = hmax2_u32(am2, hmax2_u32(r.x & 0x7FFF7FFFu, r.y & 0x7FFF7FFFu));
+      am2 = hmax2_u32(am2, hmax2_u32(r.z & 0x7FFF7FFFu, r.w & 0x7FFF7FFFu));
+    }
+  }
+  const float2 amf = __half22float2(*reinterpret_cast<const __half2*>(&am2));
+  float m = fmaxf(amf.x, amf.y);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) bars->red[x][warp & 3] = m;
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + x) : "memory");
+  m = fmaxf(fmaxf(bars->red[x][0], bars->red[x][1]), fmaxf(bars->red[x][2], bars->red[x][3]));
+  // The reduction words are reused by the next item: nobody may overwrite
+  // them before all four warps have read them.
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + x) : "memory");
+  const float scale = __fdiv_rn(m, 127.f);
+  const float rscale = __frcp_rn(scale);
+  // A zero block (scale 0) or one holding inf (scale inf) quantises to all
+  // zeros in the reference (x / scale is 0 or NaN, and NaN truncates to 0).
+  const bool finite = scale > 0.f && scale <= 3.4028235e38f;
+  const uint64_t r2 = f32x2_pack(rscale, rscale), ns2 = f32x2_pack(-scale, -scale);
+  uint8_t* q8 = smem + kOffQ8 + x * kQ8Bytes;
+#pragma unroll 2
+  for (int g = 0; g < 8; ++g) {
+    // 16 codes of dims [16g, 16g+16) = chunks 2g and 2g+1
+    const uint4 ra = *chunk(2 * g), rb = *chunk(2 * g + 1);
+    const uint32_t hw[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+    uint32_t u[16];
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hw[p]));
+      if (finite) {
+        quant_code_pair_fma(f.x, f.y, r2, ns2, &u[2 * p], &u[2 * p + 1]);
+      } else {
+        u[2 * p] = 0u;
+        u[2 * p + 1] = 0u;
+      }
+    }
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      w[i] = __byte_perm(__byte_perm(u[4 * i], u[4 * i + 1], 0x0040), __byte_perm(u[4 * i + 2], u[4 * i + 3], 0x0040),
+                         0x5410);
+    *reinterpret_cast<uint4*>(q8 + t * 128 + ((g ^ (t & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *chunk(2 * g) = make_uint4(scale_pair(hw[0]), scale_pair(hw[1]), scale_pair(hw[2]), scale_pair(hw[3]));
+    *chunk(2 * g + 1) = make_uint4(scale_pair(hw[4]), scale_pair(hw[5]), scale_pair(hw[6]), scale_pair(hw[7]));
+  }
+  fence_proxy_async_smem();
+  return __float2half_rn(scale);
+}
+
+// Write this thread's O row (128 fp32 columns in TMEM) as fp16 O / l, 16
+// columns at a time, and release the accumulator (o_free) once all of it has
+// been read. acc / l: reciprocal once per row, then per element one residual
+// correction (Markstein's method: q0 = a*r, e = a - q0*l, q = q0 + e*r), which
+// gives the correctly rounded quotient for these normal operands. Each thread
+// writes its own row (rows are a token stride apart), 32 bytes per store where
+// the layout allows.
+__device__ __forceinline__ void epilogue_o_row(uint32_t taddr, bool have_o, float l, __half* orow, bool store,
+                                               bool vec32, uint64_t* o_free) {
+  const float rl = __frcp_rn(l);
+  const uint64_t rl2 = f32x2_pack(rl, rl), nl2 = f32x2_pack(-l, -l);
+  uint4* dst = reinterpret_cast<uint4*>(orow);
+#pragma unroll 1
+  for (int c = 0; c < 8; ++c) {
+    uint32_t o[16];
+    if (have_o) {
+      tmem_ld16(taddr + 16 * c, o);
+      tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = 0u;
+    }
+    if (c == 7) {
+      tc_fence_before();
+      mbar_arrive(o_free);
+    }
+    if (store) {
+      uint32_t w[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint64_t a2 = f32x2_pack(__uint_as_float(o[2 * e]), __uint_as_float(o[2 * e + 1]));
+        const uint64_t q0 = f32x2_fma(a2, rl2, 0ull);
+        const uint64_t r = f32x2_fma(q0, nl2, a2);
+        const float2 q = f32x2_unpack(f32x2_fma(r, rl2, q0));
+        w[e] = pack_half2_rn(q.x, q.y);
+      }
+      if (vec32) {
+        asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst + 2 * c), "r"(w[0]),
+                     "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                     : "memory");
+      } else {
+        dst[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     tilemix_attn_fwd_paired_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k16,
                                    const __grid_constant__ CUtensorMap tm_k8, const __grid_constant__ CUtensorMap tm_v,
-                                   const AttnArgs a) {
+                                   const AttnArgs a, const Grid grid) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kOffBar);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.z;
-  const int q_start = a.cu_q[b];
-  const int seqlen_q = a.cu_q[b + 1] - q_start;
-  const int k_start = a.cu_k[b];
-  const int seqlen_k = a.cu_k[b + 1] - k_start;
-  const int m_blocks = (seqlen_q + kRows - 1) / kRows;
-
-  QTile tl[2];
-  const int rev = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
-#pragma unroll
-  for (int x = 0; x < 2; ++x) {
-    if (a.pair_heads) {
-      tl[x].hq = 2 * static_cast<int>(blockIdx.y) + x;
-      tl[x].mtile = rev;
-    } else {
-      tl[x].hq = blockIdx.y;
-      tl[x].mtile = 2 * rev + x;
-    }
-    const bool valid = tl[x].mtile * kRows < seqlen_q;
-    tl[x].nb = valid ? visited_key_tiles(tl[x].mtile * kRows, kRows, seqlen_q, seqlen_k, a.causal) : 0;
-    tl[x].bits = 0;
-    if (valid && a.mode == TM_ROUTE_MIXED)
-      tl[x].bits = a.bitmask[static_cast<int64_t>(tl[x].hq / a.group) * m_blocks + tl[x].mtile];
-  }
-  const bool valid0 = tl[0].mtile * kRows < seqlen_q;
-  const bool valid1 = tl[1].mtile * kRows < seqlen_q;
-  if (!valid0 && !valid1) return;  // uniform, before any barrier or allocation
-  const int hk = tl[0].hq / a.group;  // both tiles share the KV head
-  const int n_iter = max(tl[0].nb, tl[1].nb);
+  if (item_index(0, grid) < 0) return;  // uniform, before any barrier or allocation
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -133,6 +340,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->q_full[x], 1);
       mbar_init(&bars->q_ready[x], kRows);
+      mbar_init(&bars->q_empty[x], 1);
+      mbar_init(&bars->o_free[x], kRows);
       for (int s = 0; s < 2; ++s) {
         mbar_init(&bars->s_full[x][s], 1);
         mbar_init(&bars->p_ready[x][s], kRows);
@@ -154,8 +363,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 8 || warp == 10) {
     // ------------------------------------------------------------------ producers
-    // The whole warp runs the loop (warp-uniform control flow); one elected
-    // lane issues each copy.
+    // The whole warp runs the loops (warp-uniform control flow); one elected
+    // lane issues each copy. g counts key tiles over all items (ring position).
     const bool is_k = warp == 8;
     if (is_k) {
       prefetch_tmap(&tm_k16);
@@ -163,65 +372,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_v);
-#pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        if (tl[x].mtile * kRows >= seqlen_q) continue;
-        mbar_arrive_expect_tx_e(&bars->q_full[x], kQ16Bytes);
-        tma_load_4d_e(smem + kOffQ16 + x * kQ16Bytes, &tm_q, &bars->q_full[x], 0, q_start + tl[x].mtile * kRows, 0,
-                      tl[x].hq);
-      }
     }
     bool ok = true;
-    RouteWalker rw[2];
-#pragma unroll
-    for (int x = 0; x < 2; ++x) rw[x].init(a.mode, tl[x].bits, a.block_n_mask);
-    for (int j = 0; j < n_iter && ok; ++j) {
-      const int s = j % kStages;
-      if (j >= kStages)
-        ok = __all_sync(0xffffffffu, mbar_wait_spin(is_k ? &bars->empty_k[s] : &bars->empty_v[s],
-                                               ((j - kStages) / kStages) & 1, a.err, kErrTimeoutEmpty));
-      if (!ok) break;
-      const int tok = k_start + j * kKeys;
-      if (is_k) {
-        bool n16 = false, n8 = false;
+    uint32_t g = 0;
+    int n = 0;  // items done
+    ItemWalk walk;
+    Item m;
+    int it = walk.next(a, grid, m);
+    while (it >= 0 && ok) {
+      ItemWalk peek = walk;
+      Item mn;
+      const int it_next = peek.next(a, grid, mn);
+      if (!is_k) {
+        // Q tiles of this item, each once the previous item's last S of that
+        // tile has completed.
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-          if (j < tl[x].nb) {
-            if (rw[x].kind())
-              n8 = true;
-            else
-              n16 = true;
+          if (n > 0)
+            ok = ok && __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_empty[x], (n - 1) & 1, a.err, kErrTimeoutQFree));
+          if (!ok) break;
+          if (tile_valid(m, x)) {
+            mbar_arrive_expect_tx_e(&bars->q_full[x], kQ16Bytes);
+            tma_load_4d_e(smem + kOffQ16 + x * kQ16Bytes, &tm_q, &bars->q_full[x], 0,
+                          m.q_start + tile_of(m, x).mtile * kRows, 0, tile_of(m, x).hq);
+          } else if (lane == 0) {
+            mbar_arrive(&bars->q_full[x]);
           }
-          rw[x].advance();
+          __syncwarp();
         }
-        mbar_arrive_expect_tx_e(&bars->full_k[s], (n16 ? kK16Bytes : 0u) + (n8 ? kK8Bytes : 0u));
-        if (n16) tma_load_4d_e(smem + kOffK16 + s * kK16Bytes, &tm_k16, &bars->full_k[s], 0, tok, 0, hk);
-        if (n8) tma_load_3d_e(smem + kOffK8 + s * kK8Bytes, &tm_k8, &bars->full_k[s], 0, hk, tok);
-      } else {
-        mbar_arrive_expect_tx_e(&bars->full_v[s], kVBytes);
-        tma_load_4d_e(smem + kOffV + s * kVBytes, &tm_v, &bars->full_v[s], 0, tok, 0, hk);
-      }
-      if (kPrefetch > 0 && lane == 0) {
-        const int jq = j + kPrefetch;
-        if (jq < n_iter) {
-          const int ptok = k_start + jq * kKeys;
-          if (is_k) {
-            tma_prefetch_l2_4d(&tm_k16, 0, ptok, 0, hk);
-            if (a.mode != TM_ROUTE_FP16) tma_prefetch_l2_3d(&tm_k8, 0, hk, ptok);
-          } else {
-            tma_prefetch_l2_4d(&tm_v, 0, ptok, 0, hk);
-          }
+        // Warm L2 with the next item's Q tiles.
+        if (ok && it_next >= 0 && lane == 0) {
+#pragma unroll
+          for (int x = 0; x < 2; ++x)
+            if (tile_valid(mn, x)) tma_prefetch_l2_4d(&tm_q, 0, mn.q_start + tile_of(mn, x).mtile * kRows, 0, tile_of(mn, x).hq);
         }
       }
+      RouteWalker rw[2];
+#pragma unroll
+      for (int x = 0; x < 2; ++x) rw[x].init(a.mode, tile_of(m, x).bits, a.block_n_mask);
+      for (int j = 0; j < m.n_iter && ok; ++j, ++g) {
+        const uint32_t s = g % kStages;
+        if (g >= static_cast<uint32_t>(kStages))
+          ok = __all_sync(0xffffffffu, mbar_wait_spin(is_k ? &bars->empty_k[s] : &bars->empty_v[s],
+                                                      ((g / kStages) + 1) & 1, a.err, kErrTimeoutEmpty));
+        if (!ok) break;
+        const int tok = m.k_start + j * kKeys;
+        if (is_k) {
+          bool n16 = false, n8 = false;
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            if (j < tile_of(m, x).nb) {
+              if (rw[x].kind())
+                n8 = true;
+              else
+                n16 = true;
+            }
+            rw[x].advance();
+          }
+          mbar_arrive_expect_tx_e(&bars->full_k[s], (n16 ? kK16Bytes : 0u) + (n8 ? kK8Bytes : 0u));
+          if (n16) tma_load_4d_e(smem + kOffK16 + s * kK16Bytes, &tm_k16, &bars->full_k[s], 0, tok, 0, m.hk);
+          if (n8) tma_load_3d_e(smem + kOffK8 + s * kK8Bytes, &tm_k8, &bars->full_k[s], 0, m.hk, tok);
+        } else {
+          mbar_arrive_expect_tx_e(&bars->full_v[s], kVBytes);
+          tma_load_4d_e(smem + kOffV + s * kVBytes, &tm_v, &bars->full_v[s], 0, tok, 0, m.hk);
+        }
+      }
+      ++n;
+      walk = peek;
+      m = mn;
+      it = it_next;
     }
     // Drain: every copy this warp issued has landed before the CTA can exit.
-    const int first = max(0, n_iter - kStages);
-    for (int j = first; j < n_iter; ++j)
-      mbar_wait(is_k ? &bars->full_k[j % kStages] : &bars->full_v[j % kStages], (j / kStages) & 1, a.err,
+    const uint32_t first = g > static_cast<uint32_t>(kStages) ? g - kStages : 0u;
+    for (uint32_t q = first; q < g; ++q)
+      mbar_wait(is_k ? &bars->full_k[q % kStages] : &bars->full_v[q % kStages], (q / kStages) & 1, a.err,
                 kErrTimeoutDrain);
-    if (!is_k)
-      for (int x = 0; x < 2; ++x)
-        if (tl[x].mtile * kRows < seqlen_q) mbar_wait(&bars->q_full[x], 0, a.err, kErrTimeoutDrain);
   } else if (warp == 9 || warp == 11) {
     // ------------------------------------------------------------------ MMA issuers
     // One warp per query tile X (warp 9: A, warp 11: B, on different SM
@@ -229,13 +454,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // in a fixed order per key tile j:
     //   S_X(j), release K(j), PV_X(j-1), release V(j-1)
     // (a stage is free once both warps have committed its release). S_X(j)
-    // overwrites TMEM slot j&1, which P_X(j-2) occupied: PV_X(j-2) was issued
-    // earlier by the same thread and tcgen05.mma operations from one thread
-    // execute in issue order, so it has read P before S_X(j) writes the slot.
-    // Descriptors are built once; a byte offset is added as offset >> 4 to the
-    // start-address field (all shared-memory offsets here are < 256 KB).
+    // overwrites TMEM slot c&1 (c = step count of tile X over all items), which
+    // P_X(c-2) occupied: PV_X(c-2) was issued earlier by the same thread and
+    // tcgen05.mma operations from one thread execute in issue order, so it has
+    // read P before S_X writes the slot. Descriptors are built once; a byte
+    // offset is added as offset >> 4 to the start-address field (all
+    // shared-memory offsets here are < 256 KB).
     const int x = warp == 9 ? 0 : 1;
-    const QTile me = tl[x];
     constexpr uint32_t idesc_qk16 = make_idesc(1, 0, 0, 0, 128, 64);
     constexpr uint32_t idesc_qk8 = make_idesc(2, 1, 0, 0, 128, 64);
     constexpr uint32_t idesc_pv = make_idesc(1, 0, 0, 1, 128, kD);
@@ -246,59 +471,90 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t dv = make_sdesc(smem_u32(smem + kOffV), kVBytes / 2, 1024, 2);
     const uint32_t d_o = tbase + col_o(x);
     bool ok = true;
-    if (me.mtile * kRows < seqlen_q) ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_ready[x], 0, a.err, kErrTimeoutQ));
-    tc_fence_after();
-    RouteWalker rw;
-    rw.init(a.mode, me.bits, a.block_n_mask);
-    for (int j = 0; j <= n_iter && ok; ++j) {
-      if (j < n_iter) {
-        const int st = j % kStages;
-        const int kind = rw.kind();
-        rw.advance();
-        // Wait for K(j) even when this tile does not use it: the release below
-        // must not reach the stage's barrier before the other warp's release of
-        // the previous use of the stage (the copy of K(j) waited for it), or
-        // two releases from this warp could complete one phase.
-        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->full_k[st], (j / kStages) & 1, a.err, kErrTimeoutFull));
-        if (!ok) break;
-        if (j < me.nb) {
-          tc_fence_after();
-          const uint32_t d = tbase + col_s(x, j & 1);
-          if (kind == 0) {
-            const uint64_t kb = dk16 + ((st * kK16Bytes) >> 4);
-#pragma unroll
-            for (int kk = 0; kk < kD / 16; ++kk) {
-              const uint32_t off_q = ((kk >> 2) * (kQ16Bytes / 2) + (kk & 3) * 32) >> 4;
-              const uint32_t off_k = ((kk >> 2) * (kK16Bytes / 2) + (kk & 3) * 32) >> 4;
-              mma_f16_ss_e(d, dq16 + off_q, kb + off_k, idesc_qk16, kk > 0 ? 1u : 0u);
-            }
-          } else {
-            const uint64_t kb = dk8 + ((st * kK8Bytes) >> 4);
-#pragma unroll
-            for (int kk = 0; kk < kD / 32; ++kk) mma_i8_ss_e(d, dq8 + kk * 2, kb + kk * 2, idesc_qk8, kk > 0 ? 1u : 0u);
-          }
-          tc_commit_e(&bars->s_full[x][j & 1]);
-        }
-        tc_commit_e(&bars->empty_k[st]);  // this warp is done with K(j) once its S has run
-      }
-      if (j >= 1) {
-        const int jj = j - 1;
-        const int st = jj % kStages;
-        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->full_v[st], (jj / kStages) & 1, a.err, kErrTimeoutFull));
-        if (!ok) break;
-        if (jj < me.nb) {
-          ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->p_ready[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutP));
+    uint32_t g = 0;   // key tiles over all items
+    uint32_t cx = 0;  // steps of tile X over all items
+    int n = 0;
+    ItemWalk walk;
+    Item m;
+    int it = walk.next(a, grid, m);
+    while (it >= 0 && ok) {
+      ItemWalk peek = walk;
+      Item mn;
+      const int it_next = peek.next(a, grid, mn);
+      const int nb = tile_of(m, x).nb;
+      ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_ready[x], n & 1, a.err, kErrTimeoutQ));
+      tc_fence_after();
+      if (nb == 0) tc_commit_e(&bars->q_empty[x]);
+      RouteWalker rw;
+      rw.init(a.mode, tile_of(m, x).bits, a.block_n_mask);
+      for (int j = 0; j <= m.n_iter && ok; ++j) {
+        if (j < m.n_iter) {
+          const uint32_t gj = g + j;
+          const uint32_t st = gj % kStages;
+          const int kind = rw.kind();
+          rw.advance();
+          // Wait for K(j) even when this tile does not use it: the release below
+          // must not reach the stage's barrier before the other warp's release of
+          // the previous use of the stage (the copy of K(j) waited for it), or
+          // two releases from this warp could complete one phase.
+          ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->full_k[st], (gj / kStages) & 1, a.err, kErrTimeoutFull));
           if (!ok) break;
-          tc_fence_after();
-          const uint64_t vb = dv + ((st * kVBytes) >> 4);
-          const uint32_t pa = tbase + col_s(x, jj & 1);
+          if (j < nb) {
+            tc_fence_after();
+            const uint32_t c = cx + j;
+            const uint32_t d = tbase + col_s(x, c & 1);
+            if (kind == 0) {
+              const uint64_t kb = dk16 + ((st * kK16Bytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kKeys / 16; ++kk)
-            mma_f16_ts_e(d_o, pa + kk * 8, vb + ((kk * 16 * 128) >> 4), idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-          tc_commit_e(&bars->pv_done[x][jj & 1]);
+              for (int kk = 0; kk < kD / 16; ++kk) {
+                const uint32_t off_q = ((kk >> 2) * (kQ16Bytes / 2) + (kk & 3) * 32) >> 4;
+                const uint32_t off_k = ((kk >> 2) * (kK16Bytes / 2) + (kk & 3) * 32) >> 4;
+                mma_f16_ss_e(d, dq16 + off_q, kb + off_k, idesc_qk16, kk > 0 ? 1u : 0u);
+              }
+            } else {
+              const uint64_t kb = dk8 + ((st * kK8Bytes) >> 4);
+#pragma unroll
+              for (int kk = 0; kk < kD / 32; ++kk)
+                mma_i8_ss_e(d, dq8 + kk * 2, kb + kk * 2, idesc_qk8, kk > 0 ? 1u : 0u);
+            }
+            tc_commit_e(&bars->s_full[x][c & 1]);
+            // This tile's last S: its Q buffers can be refilled once it completes,
+            // while the other tile may still have key tiles to go.
+            if (j == nb - 1) tc_commit_e(&bars->q_empty[x]);
+          }
+          tc_commit_e(&bars->empty_k[st]);  // this warp is done with K(j) once its S has run
         }
-        tc_commit_e(&bars->empty_v[st]);
+        if (j >= 1) {
+          const int jj = j - 1;
+          const uint32_t gj = g + jj;
+          const uint32_t st = gj % kStages;
+          ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->full_v[st], (gj / kStages) & 1, a.err, kErrTimeoutFull));
+          if (!ok) break;
+          if (jj < nb) {
+            const uint32_t c = cx + jj;
+            // Before the last PV's wait for P (about one softmax step away):
+            // the last S has completed or is about to.
+            ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->p_ready[x][c & 1], (c >> 1) & 1, a.err, kErrTimeoutP));
+            if (ok && jj == 0 && n > 0)  // first PV overwrites O: the previous item's O must be read out
+              ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->o_free[x], (n - 1) & 1, a.err, kErrTimeoutOFree));
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t vb = dv + ((st * kVBytes) >> 4);
+            const uint32_t pa = tbase + col_s(x, c & 1);
+#pragma unroll
+            for (int kk = 0; kk < kKeys / 16; ++kk)
+              mma_f16_ts_e(d_o, pa + kk * 8, vb + ((kk * 16 * 128) >> 4), idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+            tc_commit_e(&bars->pv_done[x][c & 1]);
+          }
+          tc_commit_e(&bars->empty_v[st]);
+        }
       }
+      g += m.n_iter;
+      cx += nb;
+      ++n;
+      walk = peek;
+      m = mn;
+      it = it_next;
     }
     tc_commit_e(&bars->mma_done[x]);
     mbar_wait(&bars->mma_done[x], 0, a.err, kErrTimeoutDrain);
@@ -308,85 +564,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int x = warp >> 2;
     const int t = threadIdx.x & 127;  // row within the tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const QTile me = tl[x];
-    const bool tile_ok = me.mtile * kRows < seqlen_q;
-    if (tile_ok) {
-      const int row = me.mtile * kRows + t;
-      const bool row_ok = row < seqlen_q;
-      bool ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_full[x], 0, a.err, kErrTimeoutQ));
-      __half sq16 = __float2half_rn(1.f);
-      {
-        // Scale Q in place (elementwise, so the swizzled layout is irrelevant)
-        // and build the INT8 operand of this 128-row block.
-        uint8_t* q16 = smem + kOffQ16 + x * kQ16Bytes;
-        uint4 raw[16];
-        float amax = 0.f;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          uint4* ptr = reinterpret_cast<uint4*>(q16 + (c >> 3) * (kQ16Bytes / 2) + t * 128 + (((c & 7) ^ (t & 7)) << 4));
-          raw[c] = *ptr;
-          const __half2* h = reinterpret_cast<const __half2*>(&raw[c]);
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(h[e]);
-            if (row_ok) amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-            w[e] = pack_half2_rn(f.x * a.qk_scale, f.y * a.qk_scale);
-          }
-          *ptr = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-        if (a.mode != TM_ROUTE_FP16) {
-          float m = amax;
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          if (lane == 0) bars->red[x][warp & 3] = m;
-          asm volatile("bar.sync %0, 128;" ::"r"(1 + x) : "memory");
-          m = fmaxf(fmaxf(bars->red[x][0], bars->red[x][1]), fmaxf(bars->red[x][2], bars->red[x][3]));
-          const float scale = __fdiv_rn(m, 127.f);
-          const float rscale = __frcp_rn(scale);
-          sq16 = __float2half_rn(scale);
-          uint8_t* q8 = smem + kOffQ8 + x * kQ8Bytes;
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            // 16 codes of dims [16g, 16g+16) = raw chunks 2g and 2g+1
-            uint32_t w[4];
-#pragma unroll
-            for (int hc = 0; hc < 2; ++hc) {
-              const __half2* h = reinterpret_cast<const __half2*>(&raw[2 * g + hc]);
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const float2 f0 = __half22float2(h[2 * e]);
-                const float2 f1 = __half22float2(h[2 * e + 1]);
-                w[hc * 2 + e] = (static_cast<uint32_t>(quant_code_rcp(f0.x, scale, rscale)) & 0xFFu) |
-                                ((static_cast<uint32_t>(quant_code_rcp(f0.y, scale, rscale)) & 0xFFu) << 8) |
-                                ((static_cast<uint32_t>(quant_code_rcp(f1.x, scale, rscale)) & 0xFFu) << 16) |
-                                ((static_cast<uint32_t>(quant_code_rcp(f1.y, scale, rscale)) & 0xFFu) << 24);
-              }
-            }
-            *reinterpret_cast<uint4*>(q8 + t * 128 + ((g ^ (t & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&bars->q_ready[x]);
-      }
-
-      const int ks_base = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[b] : 0;
-      const int ks_end = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[b + 1] : 0;
-      const float kNegInf = -__int_as_float(0x7f800000);
+    const float kNegInf = -__int_as_float(0x7f800000);
+    bool ok = true;
+    uint32_t cx = 0;  // steps of tile X over all items
+    int n = 0;
+    ItemWalk walk;
+    Item m;
+    int it = walk.next(a, grid, m);
+    // Q of the first item.
+    __half sq16 = __float2half_rn(1.f);
+    if (it >= 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_full[x], 0, a.err, kErrTimeoutQ));
+      if (tile_valid(m, x)) sq16 = transform_q(smem, bars, a, x, t, warp, lane, tile_of(m, x).mtile * kRows + t < m.seqlen_q);
+      mbar_arrive(&bars->q_ready[x]);
+    }
+    while (it >= 0 && ok) {
+      // Everything the step loop and the epilogue need from the item, so that
+      // the item itself is dead during the loop.
+      const int nb = tile_of(m, x).nb;
+      const int row = tile_of(m, x).mtile * kRows + t;
+      const bool store = tile_valid(m, x) && row < m.seqlen_q;
+      __half* orow = a.out + (static_cast<int64_t>(m.q_start) + row) * a.o_st + static_cast<int64_t>(tile_of(m, x).hq) * a.o_sh;
+      int lim0 = m.seqlen_k;  // keys of this row before tile 0's end is subtracted
+      if (a.causal) lim0 = min(lim0, row + (m.seqlen_k - m.seqlen_q) + 1);
       float m_used = kNegInf;
       float l = 1.f;
-      const int coff = seqlen_k - seqlen_q;
+      const int ks_base = m.ks_base, ks_end = m.ks_end;
       // K block scale of a tile, loaded one tile ahead to keep the global load
       // off the critical path. Routes and scale blocks of consecutive tiles are
       // tracked incrementally (no per-tile division).
       RouteWalker rw;
-      rw.init(a.mode, me.bits, a.block_n_mask);
+      rw.init(a.mode, tile_of(m, x).bits, a.block_n_mask);
       const int sk_per = a.blkk / kKeys;  // 64-key tiles per K scale block (blkk % 64 == 0)
       int sk_idx = ks_base, sk_sub = 0;
       // The load is unconditional (clamped to a valid row) and its value is only
       // selected when used, one tile later, so no instruction waits on it early.
       const bool have_sk = ks_end > ks_base;
-      const __half* sk_col = a.k_scale + hk;
+      const __half* sk_col = a.k_scale + m.hk;
       auto load_next_sk = [&]() -> __half {  // raw scale of the next tile in order; then step
         const __half v = have_sk ? sk_col[static_cast<int64_t>(min(sk_idx, ks_end - 1)) * a.HK] : __half();
         if (++sk_sub == sk_per) {
@@ -396,27 +610,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         return v;
       };
       __half sk_next = load_next_sk();
-      for (int j = 0; ok && j < me.nb; ++j) {
-        const int slot = j & 1;
+      for (int j = 0; ok && j < nb; ++j) {
+        const uint32_t c = cx + j;
+        const int slot = c & 1;
         const int kind = rw.kind();
         rw.advance();
         const __half sk16 = (have_sk && kind == 1) ? sk_next : __float2half_rn(1.f);
         sk_next = load_next_sk();
         const float ss = kind == 1 ? int8_score_scale(sq16, sk16, a.qk_scale) : 1.f;
-        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->s_full[x][slot], (j >> 1) & 1, a.err, kErrTimeoutScores));
+        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->s_full[x][slot], (c >> 1) & 1, a.err, kErrTimeoutScores));
         if (!ok) break;
         tc_fence_after();
-        int lim = seqlen_k - j * kKeys;
-        if (a.causal) lim = min(lim, row + coff + 1 - j * kKeys);
+        const int lim = lim0 - j * kKeys;
         uint32_t p[32];
         float o_scale;
         bool need_rescale;
         softmax_tile(tbase + lane_off + col_s(x, slot), kind, ss, lim, a.rescale_threshold, m_used, l, p, o_scale,
                      need_rescale);
         if (__any_sync(0xffffffffu, need_rescale)) {
-          const int jj = j - 1;
-          ok = __all_sync(0xffffffffu,
-                          mbar_wait_spin(&bars->pv_done[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutPV));
+          const uint32_t cp = c - 1;
+          ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->pv_done[x][cp & 1], (cp >> 1) & 1, a.err, kErrTimeoutPV));
           if (!ok) break;
           tc_fence_after();
           rescale_o_row<kD>(tbase + lane_off + col_o(x), o_scale);
@@ -426,13 +639,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(&bars->p_ready[x][slot]);
       }
-      __half* orow = a.out + (static_cast<int64_t>(q_start) + row) * a.o_st + static_cast<int64_t>(me.hq) * a.o_sh;
-      if (ok && me.nb > 0) {
-        const int jj = me.nb - 1;
-        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->pv_done[x][jj & 1], (jj >> 1) & 1, a.err, kErrTimeoutPV));
+      if (!ok) break;
+      cx += nb;
+      ItemWalk peek = walk;
+      Item mn;
+      const int it_next = peek.next(a, grid, mn);
+      // The next item's Q (its tile landed after this item's last S of the
+      // tile) while the tensor core finishes this item's last PV.
+      __half sq16_next = __float2half_rn(1.f);
+      if (it_next >= 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_full[x], (n + 1) & 1, a.err, kErrTimeoutQ));
+        if (!ok) break;
+        if (tile_valid(mn, x))
+          sq16_next = transform_q(smem, bars, a, x, t, warp, lane, tile_of(mn, x).mtile * kRows + t < mn.seqlen_q);
+        mbar_arrive(&bars->q_ready[x]);
+      }
+      // This item's O.
+      if (nb > 0) {
+        const uint32_t cl = cx - 1;
+        ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->pv_done[x][cl & 1], (cl >> 1) & 1, a.err, kErrTimeoutPV));
         tc_fence_after();
       }
-      store_o_row<kD>(tbase + lane_off + col_o(x), me.nb > 0, l, orow, row_ok && ok);
+      epilogue_o_row(tbase + lane_off + col_o(x), nb > 0 && ok, l, orow, store && ok, a.o_vec32 != 0,
+                     &bars->o_free[x]);
+      sq16 = sq16_next;
+      ++n;
+      walk = peek;
+      m = mn;
+      it = it_next;
     }
   }
 
@@ -453,19 +687,31 @@ int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUten
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TM_ERR_LAUNCH;
   static bool attr_set[64] = {};
+  static int n_sm[64] = {};
   if (!attr_set[dev]) {
     if (cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) != cudaSuccess)
       return TM_ERR_LAUNCH;
+    if (cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm[dev] <= 0)
+      return TM_ERR_LAUNCH;
     attr_set[dev] = true;
   }
   const int mtiles = (max_seqlen_q + kRows - 1) / kRows;
-  dim3 grid;
-  if (a.pair_heads)
-    grid = dim3(mtiles, a.HQ / 2, batch);
-  else
-    grid = dim3((mtiles + 1) / 2, a.HQ, batch);
-  tilemix_attn_fwd_paired_kernel<<<grid, kThreads, kSmemBytes, stream>>>(q, k16, k8, v, a);
+  Grid g;
+  if (a.pair_heads) {
+    g.nx = mtiles;
+    g.ny = a.HQ / 2;
+  } else {
+    g.nx = (mtiles + 1) / 2;
+    g.ny = a.HQ;
+  }
+  g.nz = batch;
+  const int64_t items = static_cast<int64_t>(g.nx) * g.ny * g.nz;
+  if (items <= 0) return TM_OK;
+  if (items > (1ll << 30)) return TM_ERR_SHAPE;
+  g.n_items = static_cast<int>(items);
+  const int ctas = static_cast<int>(std::min<int64_t>(items, n_sm[dev]));
+  tilemix_attn_fwd_paired_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(q, k16, k8, v, a, g);
   return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
 }
 

@@ -30,6 +30,8 @@ enum : int {
   kErrTimeoutQ = 6,         // MMA warp waited too long for Q in TMEM
   kErrTimeoutDrain = 7,     // final drain of in-flight work timed out
   kErrTimeoutExchange = 8,  // partner thread of a split softmax row never published its value
+  kErrTimeoutQFree = 9,     // Q producer waited too long for the previous work item's last S
+  kErrTimeoutOFree = 10,    // MMA warp waited too long for the previous work item's O to be read
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
@@ -430,6 +432,40 @@ __device__ __forceinline__ int quant_code_rcp(float x, float scale, float rcp) {
   float y = fmaf(fmaf(-q0, scale, x), rcp, q0);
   y = __fadd_rn(y, y >= 0.f ? 0.5f : -0.5f);
   return __float2int_rz(y);
+}
+
+// Codes of a pair of x for a block scale, as quant_code_rcp but without the
+// conversion pipe (cvt.rzi shares the pipe with the softmax's ex2): the same
+// Markstein quotient y (on f32x2 pairs), then round half away from zero as
+// trunc(|y| + 0.5) with the sign of y restored. |y| + 0.5 equals the
+// reference's |y + (y >= 0 ? 0.5 : -0.5)| (round to nearest is symmetric); an
+// add rounded toward zero against 1.5 * 2^23 truncates it (it is >= 0 and
+// < 2^22), and adding 1.5 * 2^23 to the signed code leaves the code's two's
+// complement byte in the low mantissa bits. Requires a finite scale > 0
+// (callers treat other scales separately); x finite (a NaN x yields an
+// unspecified code instead of the reference's 0). Returns the low bytes of
+// the two codes in bits 0-7 of *c0 / *c1 (upper bits unspecified).
+__device__ __forceinline__ void quant_code_pair_fma(float x0, float x1, uint64_t r2, uint64_t nscale2, uint32_t* c0,
+                                                    uint32_t* c1) {
+  constexpr uint64_t kMagic2 = 0x4B4000004B400000ull;  // (1.5 * 2^23, 1.5 * 2^23)
+  const uint64_t x2 = (static_cast<uint64_t>(__float_as_uint(x1)) << 32) | __float_as_uint(x0);
+  uint64_t q0, e, y;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(q0) : "l"(x2), "l"(r2));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(e) : "l"(q0), "l"(nscale2), "l"(x2));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(y) : "l"(e), "l"(r2), "l"(q0));
+  const float y0 = __uint_as_float(static_cast<uint32_t>(y)), y1 = __uint_as_float(static_cast<uint32_t>(y >> 32));
+  const float b0 = __fadd_rn(fabsf(y0), 0.5f), b1 = __fadd_rn(fabsf(y1), 0.5f);
+  const uint64_t b2 = (static_cast<uint64_t>(__float_as_uint(b1)) << 32) | __float_as_uint(b0);
+  uint64_t t, k;
+  asm("add.rz.f32x2 %0, %1, %2;" : "=l"(t) : "l"(b2), "l"(kMagic2));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(k) : "l"(t), "l"(kMagic2));
+  const float k0 = copysignf(__uint_as_float(static_cast<uint32_t>(k)), y0);
+  const float k1 = copysignf(__uint_as_float(static_cast<uint32_t>(k >> 32)), y1);
+  const uint64_t ks = (static_cast<uint64_t>(__float_as_uint(k1)) << 32) | __float_as_uint(k0);
+  uint64_t u;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(u) : "l"(ks), "l"(kMagic2));
+  *c0 = static_cast<uint32_t>(u);
+  *c1 = static_cast<uint32_t>(u >> 32);
 }
 
 }  // namespace tilemix
