@@ -128,8 +128,10 @@ __device__ __forceinline__ void exp2_poly_x2(float x0, float x1, float& e0, floa
   e1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(t >> 32) << 23));
 }
 
-// Pairs of a 64-key tile whose exponentials run on the FMA pipe (8 of 32).
-__device__ __forceinline__ constexpr bool exp_on_fma(int pair) { return (pair & 3) == 3; }
+// Pairs of a 64-key tile whose exponentials run on the FMA pipe (4 of 32;
+// larger shares measured slower: the polynomial costs more issue slots than
+// the MUFU pipe it relieves).
+__device__ __forceinline__ constexpr bool exp_on_fma(int pair) { return (pair & 7) == 7; }
 
 // One softmax step over a 64-key tile for this thread's row.
 //   taddr     TMEM address (lane and first column) of the 64 score columns
@@ -231,17 +233,27 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss,
   }
 }
 
-// Rescale this thread's row of an fp32 O accumulator (D columns) in TMEM.
+// Rescale this thread's row of an fp32 O accumulator (D columns) in TMEM, 64
+// columns per load / wait round trip (the round trips, not the multiplies, set
+// its duration).
 template <int D>
 __device__ __forceinline__ void rescale_o_row(uint32_t taddr, float scale) {
+  const uint64_t s2 = f32x2_pack(scale, scale);
 #pragma unroll 1
-  for (int c = 0; c < D; c += 32) {
-    uint32_t o[32];
-    tmem_ld32(taddr + c, o);
+  for (int c = 0; c < D; c += 64) {
+    uint32_t o[64];
+    tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+    tmem_ld32(taddr + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
     tmem_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * scale);
-    tmem_st32(taddr + c, o);
+    for (int i = 0; i < 32; ++i) {
+      uint64_t v;
+      asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(v) : "l"(f32x2_pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]))), "l"(s2));
+      o[2 * i] = static_cast<uint32_t>(v);
+      o[2 * i + 1] = static_cast<uint32_t>(v >> 32);
+    }
+    tmem_st32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+    tmem_st32(taddr + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
   }
 }
 

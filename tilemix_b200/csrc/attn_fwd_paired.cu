@@ -627,6 +627,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool need_rescale;
         softmax_tile(tbase + lane_off + col_s(x, slot), kind, ss, lim, a.rescale_threshold, m_used, l, p, o_scale,
                      need_rescale);
+        // P goes out first; its store overlaps the wait for the previous PV
+        // when O has to be rescaled (PV(c-1) must have accumulated into O).
+        tmem_st32(tbase + lane_off + col_s(x, slot), p);
         if (__any_sync(0xffffffffu, need_rescale)) {
           const uint32_t cp = c - 1;
           ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->pv_done[x][cp & 1], (cp >> 1) & 1, a.err, kErrTimeoutPV));
@@ -634,7 +637,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           rescale_o_row<kD>(tbase + lane_off + col_o(x), o_scale);
         }
-        tmem_st32(tbase + lane_off + col_s(x, slot), p);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars->p_ready[x][slot]);

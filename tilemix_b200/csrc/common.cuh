@@ -123,15 +123,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
-// Polling wait for waits on the critical path: a thread suspended inside
-// try_wait resumes on the order of a thousand cycles after the phase
-// completes, while a test_wait loop sees it within a few tens of cycles (at
-// the price of issue slots). Bounded like mbar_wait.
+// Wait for waits on the critical path: a loop of try_wait without a suspend
+// hint. The hardware parks the warp inside try_wait until the phase completes
+// (or a short system time limit passes), so the waiting warp takes no issue
+// slots from the softmax warps and still resumes within about as many cycles
+// as a test_wait poll; a long suspend hint (mbar_wait) resumes far later.
+// Bounded like mbar_wait.
 __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (mbar_test(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t n = 1;; ++n) {
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     if ((n & 1023u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
       record_error(err, code);
       return false;
