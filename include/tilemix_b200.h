@@ -127,7 +127,11 @@ typedef struct tm_attn_params {
   int64_t k8_stride_tok, k8_stride_head;
   const void* k_scale; /* fp16 [sum ceil(Tk_b/blkk), heads_k] */
   const int32_t* cu_k_scale;
-  /* Quantised V for the INT8-V PV path (int8_use_fp16_v == 0). */
+  /* Quantised V for the INT8-V PV path (int8_use_fp16_v == 0 with an INT8
+   * route): an INT8-routed tile's PV is fp16(p * sv) x fp16(v8)
+   * (attention/triton/tilemix.py:449-497). v8 int8 [k_tokens, heads_k,
+   * head_dim] (16-byte rows), v_scale fp16 [sum ceil(Tk_b/blkk), heads_k] with
+   * int32 block offsets cu_v_scale, blocks of blkk keys as for K. */
   const int8_t* v8;
   int64_t v8_stride_tok, v8_stride_head;
   const void* v_scale;
@@ -136,7 +140,12 @@ typedef struct tm_attn_params {
   const int32_t* cu_seqlens_q; /* int32 [batch+1] */
   const int32_t* cu_seqlens_k; /* int32 [batch+1] */
   const uint64_t* precision_bitmask; /* uint64 [heads_k * ceil(max_seqlen_q/block_m)] */
-  const void* bias;                  /* reserved: must be NULL */
+  /* Optional additive fp16 bias, element (z, h, m, n) at bias_stride[0..3]:
+   * qk = fp16(qk + fp16(bias * fp16(log2 e))) on the unmasked keys
+   * (tilemix.py:264-272, :413-421). As in the reference, the element read is
+   * (0, hq, query position, key position): bias_stride[0] is not applied.
+   * The caller keeps it covering heads_q x max_seqlen_q x max_seqlen_k. */
+  const void* bias;
   int64_t bias_stride[4];
 
   int batch, heads_q, heads_k, head_dim;

@@ -35,7 +35,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent.parent))
 
-from tests.helpers import make_qkv  # noqa: E402
+from tests.helpers import make_bias, make_qkv  # noqa: E402
 
 PATTERNS = ["zero", "one", "band", "global", "row_rand", "align_sparse", "bigbird", "sptrans"]
 PERCENTS = [0.0, 0.25, 0.5, 0.75, 1.0]
@@ -116,22 +116,32 @@ def make_interp(ref_root: str):
 
     # quantiser fixtures
     q, k, v, cu = make_qkv([512, 300, 129], 3, 2, 128, seed=11, outliers=2)
-    for name, x, blk in [("q128", q, 128), ("k64", k, 64)]:
+    for name, x, blk in ([] if os.environ.get("TILEMIX_GOLDEN_ONLY") else [("q128", q, 128), ("k64", k, 64)]):
         x8, xs, cus = per_block_int8_single(x, cu, 512, BLK=blk, sm_scale=1.0)
         np.savez_compressed(HERE / f"interp_quant_{name}.npz", x8=x8.numpy(), scale=xs.numpy(),
                             cu_scale=cus.numpy(), checksum=checksum(x.numpy()))
         print("quant", name, flush=True)
 
     cases = [
-        # (name, lens, hq, hk, d, block_m, pattern, mode, seed, outliers)
-        ("cfg1_sptrans", [512], 4, 4, 64, 64, "sptrans", "mixed", 0, 0),
-        ("cfg1_zero", [512], 4, 4, 64, 64, "zero", "mixed", 0, 0),
-        ("cfg1_one", [512], 4, 4, 64, 64, "one", "mixed", 0, 0),
-        ("gqa128_sptrans", [256], 3, 1, 128, 128, "sptrans", "mixed", 5, 4),
-        ("gqa128_bigbird_varlen", [256, 160], 4, 2, 128, 128, "bigbird", "mixed", 7, 0),
+        # (name, lens, hq, hk, d, block_m, pattern, mode, seed, outliers, int8_use_fp16_v, bias seed or None)
+        ("cfg1_sptrans", [512], 4, 4, 64, 64, "sptrans", "mixed", 0, 0, True, None),
+        ("cfg1_zero", [512], 4, 4, 64, 64, "zero", "mixed", 0, 0, True, None),
+        ("cfg1_one", [512], 4, 4, 64, 64, "one", "mixed", 0, 0, True, None),
+        ("gqa128_sptrans", [256], 3, 1, 128, 128, "sptrans", "mixed", 5, 4, True, None),
+        ("gqa128_bigbird_varlen", [256, 160], 4, 2, 128, 128, "bigbird", "mixed", 7, 0, True, None),
+        # the INT8-V PV path (the API's default int8_use_fp16_v=False)
+        ("cfg1_sptrans_v8", [512], 4, 4, 64, 64, "sptrans", "mixed", 0, 0, False, None),
+        ("gqa128_sptrans_v8", [256, 200], 3, 1, 128, 128, "sptrans", "mixed", 5, 4, False, None),
+        # additive bias (indexed without a batch offset by the reference)
+        ("gqa128_sptrans_bias", [256, 200], 4, 2, 128, 128, "sptrans", "mixed", 9, 2, True, 21),
+        ("cfg1_one_bias_v8", [320, 192], 4, 2, 64, 64, "one", "mixed", 3, 0, False, 22),
     ]
-    for name, lens, hq, hk, d, bm, pattern, mode, seed, outl in cases:
+    only = os.environ.get("TILEMIX_GOLDEN_ONLY")  # comma-separated case names (default: all)
+    for name, lens, hq, hk, d, bm, pattern, mode, seed, outl, fp16_v, bias_seed in cases:
+        if only and name not in only.split(","):
+            continue
         q, k, v, cu = make_qkv(lens, hq, hk, d, seed=seed, outliers=outl)
+        bias = None if bias_seed is None else make_bias(len(lens), hq, max(lens), bias_seed)
         T = max(lens)
         bn = 64
         bnm = pick_mask_block_n(T, bn)
@@ -142,10 +152,12 @@ def make_interp(ref_root: str):
         o, m = tmx.tilemix_attention_with_quant(q, k, v, cu, cu, T, T, pm, block_m=bm, block_n=bn,
                                                 block_n_mask=bnm, causal=True, sm_scale=d ** -0.5,
                                                 routing_mode=mode, scalar_scales=(bm == 128 and bn == 64),
-                                                int8_use_fp16_v=True)
+                                                int8_use_fp16_v=fp16_v, bias=bias)
         np.savez_compressed(HERE / f"interp_attn_{name}.npz", out=o.numpy(), bitmask=pm.numpy().view(np.int64),
                             lens=np.array(lens), hq=hq, hk=hk, d=d, block_m=bm, block_n=bn, block_n_mask=bnm,
-                            seed=seed, outliers=outl, checksum=checksum(q.numpy(), k.numpy(), v.numpy()))
+                            seed=seed, outliers=outl, int8_use_fp16_v=fp16_v,
+                            bias_seed=-1 if bias_seed is None else bias_seed,
+                            checksum=checksum(q.numpy(), k.numpy(), v.numpy()))
         print("attn", name, m, flush=True)
 
 

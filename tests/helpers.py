@@ -24,6 +24,12 @@ def make_qkv(batch_lens, hq, hk, d, seed=0, outliers=0, outlier_scale=20.0):
     return q, k, v, cu
 
 
+def make_bias(n_seq, hq, T, seed, scale=2.0):
+    """Seeded fp16 additive bias [n_seq, hq, T, T] ~ scale * N(0, 1) (CPU tensor)."""
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn((n_seq, hq, T, T), generator=g) * scale).to(torch.float16)
+
+
 def random_bitmask(rows, seed=1):
     rng = np.random.default_rng(seed)
     words = rng.integers(0, 2**63, size=rows, dtype=np.int64).astype(np.uint64)

@@ -9,7 +9,7 @@ import pytest
 import torch
 
 from oracle import attention_oracle as ora
-from tests.helpers import err_stats, make_qkv, random_bitmask
+from tests.helpers import err_stats, make_bias, make_qkv, random_bitmask
 
 pytestmark = pytest.mark.gpu
 
@@ -18,7 +18,7 @@ MEAN_ABS = 2e-4
 
 
 def _run_case(lens, hq, hk, d, block_m, block_n=64, block_n_mask=64, mode="mixed", causal=True, seed=0,
-              outliers=0, threshold=0.0, bits_seed=1):
+              outliers=0, threshold=0.0, bits_seed=1, fp16_v=True, bias_seed=None, return_diff=False):
     from tilemix_b200.attention import tilemix as tmx
 
     q, k, v, cu = make_qkv(lens, hq, hk, d, seed=seed, outliers=outliers)
@@ -26,17 +26,21 @@ def _run_case(lens, hq, hk, d, block_m, block_n=64, block_n_mask=64, mode="mixed
     rows = hk * ((T + block_m - 1) // block_m)
     bm = random_bitmask(rows, seed=bits_seed)
     scalar = block_m == 128 and block_n == 64
+    bias = None if bias_seed is None else make_bias(len(lens), hq, T, bias_seed)
     ref = ora.tilemix_attention_with_quant(
         q.numpy(), k.numpy(), v.numpy(), cu.numpy(), cu.numpy(), T, T, bm.numpy().view(np.uint64),
         block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, causal=causal, routing_mode=mode,
-        scalar_scales=scalar, int8_use_fp16_v=True)
+        scalar_scales=scalar, int8_use_fp16_v=fp16_v, bias=None if bias is None else bias.numpy())
     dev = torch.device("cuda", 0)
     out = tmx._attention_forward(q.to(dev), k.to(dev), v.to(dev), cu.to(dev), cu.to(dev), T, T, bm.to(dev),
                                  block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, BLKQ=128, BLKK=64,
                                  causal=causal, sm_scale=None, mode=mode, scalar_scales=scalar,
-                                 int8_use_fp16_v=True, threshold=threshold)
+                                 int8_use_fp16_v=fp16_v, threshold=threshold,
+                                 bias=None if bias is None else bias.to(dev))
     torch.cuda.synchronize()
     assert tmx.device_error_code(dev) == 0
+    if return_diff:
+        return np.abs(out.float().cpu().numpy() - np.asarray(ref, dtype=np.float32))
     return err_stats(out, ref)
 
 
@@ -69,3 +73,47 @@ def test_attention_outlier_channels(cuda_device):
 def test_attention_non_causal(cuda_device):
     mx, mean = _run_case([640], 4, 2, 128, 128, mode="mixed", causal=False)
     assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+# The INT8-V PV path (int8_use_fp16_v=False, the API's default): INT8-routed
+# tiles multiply fp16(p * sv) by the int8 V codes. block_m 64 with a random map
+# routes the two 64-row halves of a 128-row tile differently (two PVs).
+V8_CASES = [
+    ([1024, 640], 6, 2, 128, 128, 64, "mixed"),
+    ([1024], 3, 1, 128, 128, 64, "int8"),
+    ([777, 64, 513], 2, 1, 64, 64, 64, "mixed"),
+    ([512], 4, 4, 64, 64, 128, "mixed"),
+]
+
+
+@pytest.mark.parametrize("lens,hq,hk,d,block_m,bnm,mode", V8_CASES)
+@pytest.mark.parametrize("threshold", [0.0, 8.0])
+def test_attention_int8_v_path_matches_oracle(cuda_device, lens, hq, hk, d, block_m, bnm, mode, threshold):
+    mx, mean = _run_case(lens, hq, hk, d, block_m, 64, bnm, mode, threshold=threshold, fp16_v=False, seed=3)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+BIAS_CASES = [
+    # (lens, hq, hk, d, block_m, mode, fp16_v)
+    ([512, 300], 4, 2, 128, 128, "mixed", True),
+    ([640], 3, 1, 128, 128, "fp16", True),
+    ([300, 257], 4, 4, 64, 64, "mixed", False),
+]
+
+
+@pytest.mark.parametrize("lens,hq,hk,d,block_m,mode,fp16_v", BIAS_CASES)
+def test_attention_bias_matches_oracle(cuda_device, lens, hq, hk, d, block_m, mode, fp16_v):
+    """A bias of 2 * N(0, 1) widens the logits, so softmax rows are peaked, and
+    a score whose exact value sits within float32 summation error of an fp16
+    midpoint can round to either side. Worked case (lens [640], head 1, row 26,
+    key 17): exact score 3.954101833, midpoint 3.9541015625 (2.7e-7 apart, one
+    fp32 ulp); the CPU's sum rounds up to 3.955078, the tensor core's down to
+    3.953125; adding the bias term 4.12890625 then gives 8.0859 against a tie
+    at 8.08203 that rounds to even (8.0781), one fp16 ulp of the logit, and the
+    row (three near-equal top weights) moves by 3.8e-3. The bound is therefore
+    the statistical one of the outlier-channel tests: mean <= 2e-4, at most
+    0.05 % of the elements over 2e-3, none over 3e-2."""
+    diff = _run_case(lens, hq, hk, d, block_m, 64, 64, mode, fp16_v=fp16_v, bias_seed=5, seed=2, return_diff=True)
+    assert diff.mean() <= MEAN_ABS, float(diff.mean())
+    assert diff.max() <= 3e-2, float(diff.max())
+    assert int((diff > MAX_ABS).sum()) <= 5e-4 * diff.size, (int((diff > MAX_ABS).sum()), diff.size)

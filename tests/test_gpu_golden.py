@@ -9,14 +9,15 @@ import numpy as np
 import pytest
 import torch
 
-from tests.helpers import make_qkv
+from tests.helpers import make_bias, make_qkv
 
 pytestmark = pytest.mark.gpu
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 MAX_ABS = 2e-3
 MEAN_ABS = 2e-4
-NAMES = ["cfg1_sptrans", "cfg1_zero", "cfg1_one", "gqa128_sptrans", "gqa128_bigbird_varlen"]
+NAMES = ["cfg1_sptrans", "cfg1_zero", "cfg1_one", "gqa128_sptrans", "gqa128_bigbird_varlen",
+         "cfg1_sptrans_v8", "gqa128_sptrans_v8", "gqa128_sptrans_bias", "cfg1_one_bias_v8"]
 
 
 @pytest.mark.parametrize("name", NAMES)
@@ -30,13 +31,17 @@ def test_attention_matches_reference_fixture(cuda_device, monkeypatch, name, thr
     hq, hk, d = int(f["hq"]), int(f["hk"]), int(f["d"])
     bm, bn, bnm = int(f["block_m"]), int(f["block_n"]), int(f["block_n_mask"])
     q, k, v, cu = make_qkv(lens, hq, hk, d, seed=int(f["seed"]), outliers=int(f["outliers"]))
+    fp16_v = bool(f["int8_use_fp16_v"]) if "int8_use_fp16_v" in f.files else True
+    bias_seed = int(f["bias_seed"]) if "bias_seed" in f.files else -1
     T = max(lens)
     pm = torch.from_numpy(f["bitmask"].copy()).view(torch.uint64).to(cuda_device)
     dev = cuda_device
+    bias = None if bias_seed < 0 else make_bias(len(lens), hq, T, bias_seed).to(dev)
     out, mode = tilemix_attention_with_quant(q.to(dev), k.to(dev), v.to(dev), cu.to(dev), cu.to(dev), T, T, pm,
                                              block_m=bm, block_n=bn, block_n_mask=bnm, causal=True,
                                              sm_scale=d ** -0.5, routing_mode="mixed",
-                                             scalar_scales=(bm == 128 and bn == 64), int8_use_fp16_v=True)
+                                             scalar_scales=(bm == 128 and bn == 64), int8_use_fp16_v=fp16_v,
+                                             bias=bias)
     torch.cuda.synchronize()
     assert device_error_code(dev) == 0
     diff = np.abs(out.float().cpu().numpy() - f["out"].astype(np.float32))

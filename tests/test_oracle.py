@@ -15,7 +15,7 @@ import torch
 from oracle import attention_oracle as ora
 from oracle.mt19937 import MT19937, randperm
 from oracle.precision_maps_oracle import make_precision_bitmask
-from tests.helpers import make_qkv
+from tests.helpers import make_bias, make_qkv
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
@@ -65,19 +65,31 @@ def test_quant_oracle_matches_interpreter(name, blk):
     assert np.array_equal(cus, f["cu_scale"])
 
 
-@pytest.mark.parametrize("name", ["cfg1_sptrans", "cfg1_zero", "cfg1_one", "gqa128_sptrans",
-                                  "gqa128_bigbird_varlen"])
+ATTN_FIXTURES = ["cfg1_sptrans", "cfg1_zero", "cfg1_one", "gqa128_sptrans", "gqa128_bigbird_varlen",
+                 "cfg1_sptrans_v8", "gqa128_sptrans_v8", "gqa128_sptrans_bias", "cfg1_one_bias_v8"]
+
+
+def fixture_options(f):
+    """(int8_use_fp16_v, bias seed or None) of an attention fixture (older fixtures: FP16 V, no bias)."""
+    fp16_v = bool(f["int8_use_fp16_v"]) if "int8_use_fp16_v" in f.files else True
+    bias_seed = int(f["bias_seed"]) if "bias_seed" in f.files else -1
+    return fp16_v, (None if bias_seed < 0 else bias_seed)
+
+
+@pytest.mark.parametrize("name", ATTN_FIXTURES)
 def test_attention_oracle_matches_interpreter(name):
     f = np.load(GOLDEN / f"interp_attn_{name}.npz")
     lens = [int(x) for x in f["lens"]]
     hq, hk, d = int(f["hq"]), int(f["hk"]), int(f["d"])
     bm, bn, bnm = int(f["block_m"]), int(f["block_n"]), int(f["block_n_mask"])
     q, k, v, cu = make_qkv(lens, hq, hk, d, seed=int(f["seed"]), outliers=int(f["outliers"]))
+    fp16_v, bias_seed = fixture_options(f)
     T = max(lens)
+    bias = None if bias_seed is None else make_bias(len(lens), hq, T, bias_seed).numpy()
     out = ora.tilemix_attention_with_quant(
         q.numpy(), k.numpy(), v.numpy(), cu.numpy(), cu.numpy(), T, T, f["bitmask"].view(np.uint64),
         block_m=bm, block_n=bn, block_n_mask=bnm, causal=True, sm_scale=d ** -0.5, routing_mode="mixed",
-        scalar_scales=(bm == 128 and bn == 64), int8_use_fp16_v=True)
+        scalar_scales=(bm == 128 and bn == 64), int8_use_fp16_v=fp16_v, bias=bias)
     assert np.array_equal(out.view(np.uint16), f["out"].view(np.uint16))
 
 

@@ -167,8 +167,8 @@ def _ptr(t: Optional[torch.Tensor]) -> ctypes.c_void_p:
 
 
 def _launch(q, k, v, o, cu_q, cu_k, bitmask, max_q, max_k, *, q8=None, sq=None, cuqs=None, k8=None, sk=None,
-            cuks=None, block_m, block_n, block_n_mask, BLKQ, BLKK, causal, sm_scale, mode_code, scalar_scales,
-            int8_use_fp16_v, threshold=None) -> None:
+            cuks=None, v8=None, sv=None, cuvs=None, bias=None, block_m, block_n, block_n_mask, BLKQ, BLKK, causal,
+            sm_scale, mode_code, scalar_scales, int8_use_fp16_v, threshold=None) -> None:
     p = TmAttnParams()
     p.q, p.k, p.v = _ptr(q), _ptr(k), _ptr(v)
     p.q_stride_tok, p.q_stride_head = q.stride(0), q.stride(1)
@@ -185,6 +185,14 @@ def _launch(q, k, v, o, cu_q, cu_k, bitmask, max_q, max_k, *, q8=None, sq=None, 
         p.k8 = _ptr(k8)
         p.k8_stride_tok, p.k8_stride_head = k8.stride(0), k8.stride(1)
         p.k_scale, p.cu_k_scale = _ptr(sk), _ptr(cuks)
+    if v8 is not None:
+        p.v8 = _ptr(v8)
+        p.v8_stride_tok, p.v8_stride_head = v8.stride(0), v8.stride(1)
+        p.v_scale, p.cu_v_scale = _ptr(sv), _ptr(cuvs)
+    if bias is not None:
+        p.bias = _ptr(bias)
+        for i in range(4):
+            p.bias_stride[i] = bias.stride(i)
     p.cu_seqlens_q, p.cu_seqlens_k = _ptr(cu_q), _ptr(cu_k)
     p.precision_bitmask = _ptr(bitmask)
     p.batch = cu_q.numel() - 1
@@ -209,7 +217,8 @@ def _launch(q, k, v, o, cu_q, cu_k, bitmask, max_q, max_k, *, q8=None, sq=None, 
     check(rc, "tm_attn_fwd")
 
 
-def _check_kernel_support(q, block_m, block_n, BLKK, int8_path: bool, int8_use_fp16_v: bool, bias) -> None:
+def _check_kernel_support(q, block_m, block_n, BLKK, int8_path: bool, int8_use_fp16_v: bool, bias,
+                          max_q: int = 0, max_k: int = 0) -> None:
     if q.dtype != torch.float16:
         raise TypeError("the sm_100a TileMix kernel computes in fp16; q, k and v must be torch.float16")
     if q.shape[-1] not in (64, 128):
@@ -219,10 +228,14 @@ def _check_kernel_support(q, block_m, block_n, BLKK, int8_path: bool, int8_use_f
     if int8_path and BLKK % 64 != 0:
         raise ValueError("the sm_100a TileMix kernel needs BLKK to be a multiple of 64")
     if bias is not None:
-        raise NotImplementedError("additive bias is not implemented by the sm_100a TileMix kernel")
-    if int8_path and not int8_use_fp16_v:
-        raise NotImplementedError("the INT8-V PV path (int8_use_fp16_v=False) is not implemented by the "
-                                  "sm_100a TileMix kernel; pass int8_use_fp16_v=True")
+        # The kernel reads bias[0, hq, row, key] (the reference indexes it without a batch offset) and only
+        # inside the tensor; the reference would read past a smaller bias.
+        if bias.dtype != torch.float16:
+            raise NotImplementedError("the sm_100a TileMix kernel takes an fp16 bias")
+        if bias.device != q.device:
+            raise ValueError("bias must be on q.device")
+        if bias.ndim != 4 or bias.shape[1] < q.shape[1] or bias.shape[2] < max_q or bias.shape[3] < max_k:
+            raise ValueError("bias must be [batch, heads_q, >= max_seqlen_q, >= max_seqlen_k]")
 
 
 @torch.no_grad()
@@ -287,15 +300,18 @@ def launch_prequantized(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q: int,
     if padded_head_dim > 128:
         raise ValueError("head dimension must be <= 128")
     int8_path = mode_code != ROUTING_MODE_FP16
-    _check_kernel_support(q, block_m, block_n, BLKK, int8_path, int8_use_fp16_v, bias)
+    _check_kernel_support(q, block_m, block_n, BLKK, int8_path, int8_use_fp16_v, bias, max_seqlens_q, max_seqlens_k)
     kw = {}
     if int8_path:
         kw = dict(q8=q8, sq=sQ_blocks.to(torch.float16).contiguous(), cuqs=cu_q_scale.to(torch.int32).contiguous(),
                   k8=k8, sk=sK_blocks.to(torch.float16).contiguous(), cuks=cu_k_scale.to(torch.int32).contiguous())
+        if not int8_use_fp16_v:
+            kw.update(v8=v8, sv=sV_blocks.to(torch.float16).contiguous(),
+                      cuvs=cu_v_scale.to(torch.int32).contiguous())
     _launch(q, k, v, o, cu_seqlens_q, cu_seqlens_k, precision_bitmask, max_seqlens_q, max_seqlens_k,
             block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, BLKQ=BLKQ, BLKK=BLKK, causal=causal,
             sm_scale=sm_scale, mode_code=mode_code, scalar_scales=scalar_scales,
-            int8_use_fp16_v=int8_use_fp16_v, **kw)
+            int8_use_fp16_v=int8_use_fp16_v, bias=bias, **kw)
     return o, normalized_mode
 
 
@@ -322,7 +338,7 @@ def _attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q, max_s
                        int8_use_fp16_v, bias=None, equal_len: Optional[int] = None, o=None, threshold=None):
     mode_code = _routing_mode_code(mode)
     int8_path = mode_code != ROUTING_MODE_FP16
-    _check_kernel_support(q, block_m, block_n, BLKK, int8_path, int8_use_fp16_v, bias)
+    _check_kernel_support(q, block_m, block_n, BLKK, int8_path, int8_use_fp16_v, bias, max_seqlens_q, max_seqlens_k)
     if sm_scale is None:
         sm_scale = q.shape[-1] ** -0.5
     if o is None:
@@ -337,10 +353,14 @@ def _attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q, max_s
         if BLKQ != 128:
             q8, sq, cuq = per_block_int8_single(q, cu_q, max_seqlens_q, BLK=BLKQ, sm_scale=1.0)
             kw.update(q8=q8, sq=sq.to(torch.float16).contiguous(), cuqs=cuq.to(torch.int32).contiguous())
+        if not int8_use_fp16_v:
+            # V per BLKK block as K (tilemix.py:45-107): the INT8-V PV path of INT8-routed tiles.
+            v8, sv16, cuvs = _quantize_k(v, cu_k, max_seqlens_k, BLKK, equal_len)
+            kw.update(v8=v8, sv=sv16, cuvs=cuvs)
     _launch(q, k, v, o, cu_q, cu_k, bm, max_seqlens_q, max_seqlens_k, block_m=block_m, block_n=block_n,
             block_n_mask=block_n_mask, BLKQ=BLKQ, BLKK=BLKK, causal=causal, sm_scale=sm_scale,
             mode_code=mode_code, scalar_scales=scalar_scales, int8_use_fp16_v=int8_use_fp16_v,
-            threshold=threshold, **kw)
+            threshold=threshold, bias=bias, **kw)
     return o
 
 

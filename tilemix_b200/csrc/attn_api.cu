@@ -19,7 +19,8 @@
 
 namespace tilemix {
 
-int launch_attn_general(const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v, const AttnArgs& a,
+int launch_attn_general(const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v, const CUtensorMap& v8,
+                        const AttnArgs& a,
                         int tiles, int heads_q, int batch, cudaStream_t stream);
 int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
                        const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
@@ -100,8 +101,6 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   if (p->block_n <= 0 || p->block_n % 64 != 0) return TM_ERR_UNSUPPORTED;
   if (p->block_n_mask <= 0 || p->block_n_mask % p->block_n != 0) return TM_ERR_SHAPE;
   if (p->routing_mode < 0 || p->routing_mode > 2) return TM_ERR_SHAPE;
-  if (p->bias != nullptr) return TM_ERR_UNSUPPORTED;
-  if (p->routing_mode != TM_ROUTE_FP16 && !p->int8_use_fp16_v) return TM_ERR_UNSUPPORTED;
   if (rescale_threshold < 0.f || rescale_threshold > 15.f) return TM_ERR_SHAPE;
   if (p->routing_mode == TM_ROUTE_MIXED && p->precision_bitmask == nullptr) return TM_ERR_NULL;
   const bool need_int8 = p->routing_mode != TM_ROUTE_FP16;
@@ -112,6 +111,10 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
     if (fuse_q && p->blkq != 128) return TM_ERR_UNSUPPORTED;
     if (!fuse_q && (p->q_scale == nullptr || p->cu_q_scale == nullptr || p->blkq <= 0)) return TM_ERR_NULL;
   }
+  // INT8-V PV path: INT8-routed tiles multiply fp16(p * sv) by fp16(v8) (:449-497).
+  const bool v8_path = need_int8 && !p->int8_use_fp16_v;
+  if (v8_path && (p->v8 == nullptr || p->v_scale == nullptr || p->cu_v_scale == nullptr)) return TM_ERR_NULL;
+  if (p->bias != nullptr && reinterpret_cast<uintptr_t>(p->bias) % 2 != 0) return TM_ERR_ALIGN;
   if (p->batch == 0 || p->max_seqlen_q == 0) return TM_OK;
   if (p->max_seqlen_k > 0 && (p->max_seqlen_k + p->block_n_mask - 1) / p->block_n_mask > 64) return TM_ERR_SHAPE;
   // Alignment: 16-byte rows for TMA and vector loads/stores.
@@ -125,6 +128,8 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
     if (!fuse_q && (!aligned16(p->q8) || p->q8_stride_tok % 16 != 0 || p->q8_stride_head % 16 != 0))
       return TM_ERR_ALIGN;
   }
+  if (v8_path && (!aligned16(p->v8) || p->v8_stride_tok % 16 != 0 || p->v8_stride_head % 16 != 0))
+    return TM_ERR_ALIGN;
   const int D = p->head_dim;
   CUtensorMap m_k16, m_k8, m_v;
   int rc = make_map(&m_k16, p->k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, p->heads_k, p->k_tokens, p->k_stride_head,
@@ -139,6 +144,12 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
     if (rc != TM_OK) return rc;
   } else {
     m_k8 = m_k16;  // never read
+  }
+  CUtensorMap m_v8 = m_k8;  // read only on the INT8-V path
+  if (v8_path) {
+    rc = make_map(&m_v8, p->v8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, p->heads_k, p->k_tokens, p->v8_stride_head,
+                  p->v8_stride_tok, D, D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc != TM_OK) return rc;
   }
 
   AttnArgs a;
@@ -175,11 +186,20 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   a.rescale_threshold = rescale_threshold;
   a.err = p->error_flag;
   a.sched = p->sched_workspace;
+  a.v8_path = v8_path ? 1 : 0;
+  a.v_scale = static_cast<const __half*>(p->v_scale);
+  a.cu_vs = p->cu_v_scale;
+  a.bias = static_cast<const __half*>(p->bias);
+  a.b_sh = p->bias_stride[1];
+  a.b_sm = p->bias_stride[2];
+  a.b_sn = p->bias_stride[3];
 
   a.pair_heads = (a.group % 2 == 0) ? 1 : 0;
   if (p->heads_q > 65535 || p->batch > 65535) return TM_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool paired_ok = !force_general && D == 128 && p->block_m == 128 && (fuse_q || !need_int8);
+  // Bias and the INT8-V path run on the general kernel.
+  const bool paired_ok = !force_general && D == 128 && p->block_m == 128 && (fuse_q || !need_int8) && !v8_path &&
+                         p->bias == nullptr;
   if (paired_ok && kernel_choice == 2) {
     CUtensorMap m_q;
     rc = make_map(&m_q, p->q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, p->heads_q, p->q_tokens, p->q_stride_head,
@@ -201,7 +221,7 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
     return launch_attn_paired(q4, k4, m_k8, v4, a, p->batch, p->max_seqlen_q, st);
   }
   const int tiles = (p->max_seqlen_q + 127) / 128;
-  return launch_attn_general(m_k16, m_k8, m_v, a, tiles, p->heads_q, p->batch, st);
+  return launch_attn_general(m_k16, m_k8, m_v, m_v8, a, tiles, p->heads_q, p->batch, st);
 }
 
 extern "C" const char* tm_status_string(int status) {

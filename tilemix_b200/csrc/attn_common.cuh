@@ -44,6 +44,14 @@ struct AttnArgs {
   float rescale_threshold;
   int* err;
   int* sched;  // dynamic scheduler counters (int[2]) of the persistent kernel
+  // INT8-V PV path (int8_use_fp16_v == 0, general kernel): fp16 V block scales.
+  int v8_path;
+  const __half* v_scale;
+  const int32_t* cu_vs;
+  // Additive fp16 bias [., HQ, Tq, Tk] (general kernel); no batch offset, as
+  // the reference indexes it (tilemix.py:264-270).
+  const __half* bias;
+  int64_t b_sh, b_sm, b_sn;
 };
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
@@ -143,9 +151,13 @@ __device__ __forceinline__ constexpr bool exp_on_fma(int pair) { return (pair & 
 // O accumulator row has to be multiplied by o_scale before this P is added.
 // The row maximum is taken over the fp32 values before their fp16 rounding:
 // rounding to nearest is monotonic, so fp16(max v) = max fp16(v).
+//   brow      optional additive bias of this row and tile (element i at
+//             brow[i * bstride]): qk = fp16(qk + fp16(b * fp16(log2 e))) on the
+//             valid keys (tilemix.py:264-272, :413-421)
 __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss, int lim, float thr,
                                              float& m_used, float& l, uint32_t (&p)[32], float& o_scale,
-                                             bool& need_rescale) {
+                                             bool& need_rescale, const __half* brow = nullptr,
+                                             int64_t bstride = 0) {
   uint32_t s[64];
   tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
   tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
@@ -169,6 +181,21 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss,
 #pragma unroll
     for (int i = 0; i < 64; ++i)
       if (i >= lim) s[i] = 0xFF800000u;  // -inf
+  }
+  if (brow != nullptr) {
+    // fp16 products and sums, each rounded once: fp32 holds the exact product
+    // of two fp16 values, and a sum of two fp16 values rounded to fp32 and then
+    // to fp16 is the correctly rounded fp16 sum (24 >= 2 * 11 + 2 bits).
+    const float l2e = __half2float(__float2half_rn(1.4426950408889634f));
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      if (i < lim) {
+        const float b = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(brow) + i * bstride)));
+        const float bb = __half2float(__float2half_rn(b * l2e));
+        const float q16 = __half2float(__float2half_rn(__uint_as_float(s[i])));
+        s[i] = __float_as_uint(__half2float(__float2half_rn(q16 + bb)));
+      }
+    }
   }
   // Row maximum: a tree of 3-input maxima (64 -> 22 -> 8 -> 4 -> 2 -> 1).
   float m1[22];

@@ -23,6 +23,18 @@
 // S/P live in three 64-column TMEM slots so that QK^T of tile j+1 and PV of
 // tile j-1 run on the tensor core while the softmax works on tile j.
 //
+// INT8-V PV path (int8_use_fp16_v == 0, tilemix.py:449-497): an INT8-routed
+// tile's PV is fp16(p * sv) x fp16(v8) with sv the V block scale. The producer
+// also loads the tile's int8 V; the softmax warps, which see the stage landed
+// once its S is complete, write the exact fp16 copy of it into a second fp16
+// V buffer of the stage before they publish P. When the two 64-row halves of
+// a block_m 64 tile take different routes, P of the FP16 half goes to the
+// slot's first 32 columns and P of the INT8 half to the next 32, and the MMA
+// warp issues one PV against V and one against the converted V8.
+// Additive bias (tilemix.py:264-272): added to the fp16 scores of the valid
+// keys before the row maximum, indexed without a batch offset as the
+// reference does.
+//
 // Rescaling of O: with rescale_threshold == 0 the running max is updated on
 // every increase exactly as in the reference. With a positive threshold t
 // (log2 units) the reference max is only moved when the tile max exceeds it by
@@ -52,10 +64,14 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kK16Bytes = 64 * 128 * 2;  // one stage of fp16 K (head_dim <= 128)
 constexpr uint32_t kK8Bytes = 64 * 128;       // one stage of int8 K
 constexpr uint32_t kVBytes = 64 * 128 * 2;    // one stage of fp16 V
+constexpr uint32_t kV8Bytes = 64 * 128;       // one stage of int8 V (INT8-V path)
+constexpr uint32_t kV8FBytes = 64 * 128 * 2;  // its fp16 copy, in the layout of a V stage
 constexpr uint32_t kOffK16 = 0;
 constexpr uint32_t kOffV = kOffK16 + kStages * kK16Bytes;
 constexpr uint32_t kOffK8 = kOffV + kStages * kVBytes;
-constexpr uint32_t kOffBar = kOffK8 + kStages * kK8Bytes;
+constexpr uint32_t kOffV8 = kOffK8 + kStages * kK8Bytes;
+constexpr uint32_t kOffV8F = kOffV8 + kStages * kV8Bytes;
+constexpr uint32_t kOffBar = kOffV8F + kStages * kV8FBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // barriers + alignment slack
 
 
@@ -96,10 +112,50 @@ struct Route {
 
 __device__ __forceinline__ void named_bar_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Four int8 in a word -> two fp16 pairs, exactly: the byte b + 128 placed in
+// the mantissa of 1024.0 gives the fp16 value 1024 + (b + 128); subtracting
+// 1152 leaves b.
+__device__ __forceinline__ void int8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t x = w ^ 0x80808080u;
+  const __half2 off = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152.0
+  uint32_t a = __byte_perm(x, 0x64646464u, 0x5140), b = __byte_perm(x, 0x64646464u, 0x7362);
+  const __half2 ha = __hsub2(*reinterpret_cast<const __half2*>(&a), off);
+  const __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&b), off);
+  lo = *reinterpret_cast<const uint32_t*>(&ha);
+  hi = *reinterpret_cast<const uint32_t*>(&hb);
+}
+
+// The int8 V tile of ring stage s (TMA layout: D bytes per key row, 128- or
+// 64-byte swizzle) -> its fp16 copy in the layout of a V stage (64-dim boxes
+// of 128-byte rows, 128-byte swizzle). Called by the 128 softmax threads.
+template <int D>
+__device__ __forceinline__ void convert_v8_stage(uint8_t* smem, int s, int t) {
+  const uint8_t* src = smem + kOffV8 + s * kV8Bytes;
+  uint8_t* dst = smem + kOffV8F + s * kV8FBytes;
+  constexpr int kChunks = D / 16;  // 16-byte int8 chunks per key row
+#pragma unroll
+  for (int u = t; u < 64 * kChunks; u += 128) {
+    const int r = u / kChunks, c = u % kChunks;
+    const int pos = (D == 128) ? (c ^ (r & 7)) : (c ^ ((r >> 1) & 3));
+    const uint4 w = *reinterpret_cast<const uint4*>(src + r * D + (pos << 4));
+    uint32_t h[8];
+    int8x4_to_f16x4(w.x, h[0], h[1]);
+    int8x4_to_f16x4(w.y, h[2], h[3]);
+    int8x4_to_f16x4(w.z, h[4], h[5]);
+    int8x4_to_f16x4(w.w, h[6], h[7]);
+    // dims 16c .. 16c+15 = 8-dim fp16 chunks cb, cb+1 of 64-dim box (16c)/64
+    const int box = (16 * c) / 64, cb = ((16 * c) % 64) / 8;
+    uint8_t* row = dst + box * (64 * 64 * 2) + r * 128;
+    *reinterpret_cast<uint4*>(row + ((cb ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(row + (((cb + 1) ^ (r & 7)) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+  }
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     tilemix_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_k16, const __grid_constant__ CUtensorMap tm_k8,
-                            const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+                            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_v8,
+                            const AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kOffBar);
@@ -168,6 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tm_k16);
       prefetch_tmap(&tm_v);
       if (a.mode != TM_ROUTE_FP16) prefetch_tmap(&tm_k8);
+      if (a.v8_path) prefetch_tmap(&tm_v8);
       bool ok = true;
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int s = j % kStages;
@@ -175,16 +232,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         bool n16, n8;
         rt.needs(j, n16, n8);
+        const bool use_v8 = a.v8_path && n8;     // INT8-routed rows take int8 V
+        const bool use_v16 = !a.v8_path || n16;  // the others the fp16 V
         const uint32_t vbytes = static_cast<uint32_t>(D) * 64 * 2;
-        const uint32_t bytes = vbytes + (n16 ? vbytes : 0u) + (n8 ? static_cast<uint32_t>(D) * 64 : 0u);
+        const uint32_t bytes = (use_v16 ? vbytes : 0u) + (n16 ? vbytes : 0u) +
+                               (n8 ? static_cast<uint32_t>(D) * 64 : 0u) + (use_v8 ? static_cast<uint32_t>(D) * 64 : 0u);
         mbar_arrive_expect_tx(&bars->full[s], bytes);
         const int tok = k_start + j * kKeys;
 #pragma unroll
         for (int box = 0; box < D / 64; ++box) {
           if (n16) tma_load_3d(smem + kOffK16 + s * kK16Bytes + box * k16_box_bytes, &tm_k16, &bars->full[s], box * 64, hk, tok);
-          tma_load_3d(smem + kOffV + s * kVBytes + box * k16_box_bytes, &tm_v, &bars->full[s], box * 64, hk, tok);
+          if (use_v16) tma_load_3d(smem + kOffV + s * kVBytes + box * k16_box_bytes, &tm_v, &bars->full[s], box * 64, hk, tok);
         }
         if (n8) tma_load_3d(smem + kOffK8 + s * kK8Bytes, &tm_k8, &bars->full[s], 0, hk, tok);
+        if (use_v8) tma_load_3d(smem + kOffV8 + s * kV8Bytes, &tm_v8, &bars->full[s], 0, hk, tok);
       }
       // Drain: every issued copy must land before the CTA exits.
       const int first = max(0, n_tiles - kStages);
@@ -242,11 +303,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = mbar_wait(&bars->p_ready[slot], (jj / kSlots) & 1, a.err, kErrTimeoutP);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t vbase = smem_u32(smem + kOffV + s * kVBytes);
           const uint32_t p_col = kColS + slot * 64;
-          for (int kk = 0; kk < kKeys / 16; ++kk) {
-            const uint64_t bdesc = make_sdesc(vbase + kk * 16 * 128, k16_box_bytes, 1024, 2);
-            mma_f16_ts(tbase + kColO, tbase + p_col + kk * 8, bdesc, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          bool pn16, pn8;
+          rt.needs(jj, pn16, pn8);
+          const bool pv8 = a.v8_path && pn8;
+          // PV against V (FP16 rows, or all rows off the INT8-V path), then
+          // against the converted int8 V (from P's second 32 columns when the
+          // halves of the tile were routed differently).
+          const int groups = (pv8 && pn16) ? 2 : 1;
+          for (int g = 0; g < groups; ++g) {
+            const bool use_v8f = pv8 && (g == 1 || !pn16);
+            const uint32_t vbase = smem_u32(smem + (use_v8f ? kOffV8F + s * kV8FBytes : kOffV + s * kVBytes));
+            const uint32_t pcol = p_col + (g == 1 ? 32u : 0u);
+            for (int kk = 0; kk < kKeys / 16; ++kk) {
+              const uint64_t bdesc = make_sdesc(vbase + kk * 16 * 128, k16_box_bytes, 1024, 2);
+              mma_f16_ts(tbase + kColO, tbase + pcol + kk * 8, bdesc, idesc_pv, (jj > 0 || kk > 0 || g > 0) ? 1u : 0u);
+            }
           }
           tc_commit(&bars->pv_done[slot]);
           tc_commit(&bars->empty[s]);
@@ -345,6 +417,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int ks_base = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[b] : 0;
     const int ks_end = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[b + 1] : 0;
+    const int vs_base = a.v8_path ? a.cu_vs[b] : 0;
+    const int vs_end = a.v8_path ? a.cu_vs[b + 1] : 0;
+    const __half* brow0 = (a.bias != nullptr && row_ok)
+                              ? a.bias + static_cast<int64_t>(hq) * a.b_sh + static_cast<int64_t>(row) * a.b_sm
+                              : nullptr;
     const float kNegInf = -__int_as_float(0x7f800000);
     float m_used = kNegInf;
     float l = 1.f;
@@ -377,8 +454,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (active) {
         int lim = seqlen_k - j * kKeys;
         if (a.causal) lim = min(lim, row + coff + 1 - j * kKeys);
+        const __half* brow = brow0 ? brow0 + static_cast<int64_t>(j) * kKeys * a.b_sn : nullptr;
         softmax_tile(tbase + lane_off + src_col, kind, ss, lim, a.rescale_threshold, m_used, l, p, o_scale,
-                     need_rescale);
+                     need_rescale, brow, a.b_sn);
+        if (kind == 1 && a.v8_path) {
+          // p_scaled = fp16(p * sv), sv the V scale of the tile's block (:472-480)
+          __half sv = __float2half_rn(1.f);
+          if (vs_end > vs_base) sv = a.v_scale[static_cast<int64_t>(min(vs_base + (j * kKeys) / a.blkk, vs_end - 1)) * a.HK + hk];
+          const float svf = __half2float(sv);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&p[i]));
+            p[i] = pack_half2_rn(f.x * svf, f.y * svf);
+          }
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) p[i] = 0u;
@@ -392,7 +481,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         rescale_o_row<D>(tbase + lane_off + kColO, o_scale);
       }
-      tmem_st32(tbase + lane_off + kColS + slot * 64, p);
+      if (a.v8_path && n8) {
+        // The int8 V of this tile (landed: its S is complete) as fp16 for the PV.
+        convert_v8_stage<D>(smem, j % kStages, t);
+        fence_proxy_async_smem();
+      }
+      if (a.v8_path && n8 && n16) {
+        // Split tile: P of FP16-routed rows in columns [0, 32), of INT8-routed
+        // rows in [32, 64); the other half of each row is zero.
+        const bool int8_row = active && kind == 1;
+        uint32_t pa[32], pb[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          pa[i] = int8_row ? 0u : p[i];
+          pb[i] = int8_row ? p[i] : 0u;
+        }
+        tmem_st32(tbase + lane_off + kColS + slot * 64, pa);
+        tmem_st32(tbase + lane_off + kColS + slot * 64 + 32, pb);
+      } else {
+        tmem_st32(tbase + lane_off + kColS + slot * 64, p);
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->p_ready[slot]);
@@ -421,7 +529,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace general
 
 // Launch the general kernel (any supported block_m, head_dim 64/128, prequantised or fused Q).
-int launch_attn_general(const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v, const AttnArgs& a,
+int launch_attn_general(const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v, const CUtensorMap& v8,
+                        const AttnArgs& a,
                         int tiles, int heads_q, int batch, cudaStream_t stream) {
   using namespace general;
   int dev = 0;
@@ -437,9 +546,9 @@ int launch_attn_general(const CUtensorMap& k16, const CUtensorMap& k8, const CUt
   }
   dim3 grid(tiles, heads_q, batch);
   if (a.D == 128)
-    tilemix_attn_fwd_kernel<128><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, a);
+    tilemix_attn_fwd_kernel<128><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, v8, a);
   else
-    tilemix_attn_fwd_kernel<64><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, a);
+    tilemix_attn_fwd_kernel<64><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, v8, a);
   return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
 }
 
