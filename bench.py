@@ -443,6 +443,58 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def run_prefill_components(args) -> None:
+    """--component prefill: the Llama prefill companions at the workload's shapes (8 x 4096
+    tokens of Llama-3.2-3B: hidden 3072, 24 / 8 heads of 128, MLP 8192), each timed with CUDA
+    events over --steps launches after --warmup, against the measured HBM copy peak. One
+    JSON line; the default bench line is unaffected."""
+    import torch
+
+    from tilemix_b200.models.tilemix_llama import rms_norm, rotary_token_major, rotary_token_major_quant_k, silu_mul
+
+    dev = torch.device("cuda", 0)
+    B, T, HQ, HK, D, HID, MLP = CFG["batch"], CFG["seq_len"], CFG["heads_q"], CFG["heads_k"], CFG["head_dim"], 3072, 8192
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = torch.randn((B, T, (HQ + 2 * HK) * D), device=dev, generator=g).half()
+    q = qkv[..., : HQ * D].view(B, T, HQ, D).transpose(1, 2)
+    k = qkv[..., HQ * D:(HQ + HK) * D].view(B, T, HK, D).transpose(1, 2)
+    cos = torch.randn((1, T, D), device=dev, generator=g).half()
+    sin = torch.randn((1, T, D), device=dev, generator=g).half()
+    gate = torch.randn((B, T, MLP), device=dev, generator=g).half()
+    up = torch.randn((B, T, MLP), device=dev, generator=g).half()
+    x = torch.randn((B, T, HID), device=dev, generator=g).half()
+    w = torch.rand((HID,), device=dev, generator=g).half()
+    peaks, src = load_peaks()
+    tok = B * T
+    rope_bytes = 2 * tok * (HQ + HK) * D * 2 + 2 * T * D * 2
+    cases = [
+        ("rotary_token_major", lambda: rotary_token_major(q, k, cos, sin), rope_bytes),
+        ("rotary_token_major_quant_k", lambda: rotary_token_major_quant_k(q, k, cos, sin, 64),
+         rope_bytes + tok * HK * D + tok // 64 * HK * 2),
+        ("silu_mul", lambda: silu_mul(gate, up), 3 * tok * MLP * 2),
+        ("rms_norm", lambda: rms_norm(x, w, 1e-5), 2 * tok * HID * 2 + HID * 2),
+    ]
+    out = []
+    for name, fn, nbytes in cases:
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out.append({"kernel": name, "ms": ms, "algorithmic_bytes": nbytes, "achieved_gbs": gbs,
+                    "peak_gbs": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"]})
+    print(json.dumps({"component": "prefill companions", "bound": "hbm", "peak_source": f"hbm_gbs of {src}",
+                      "config": {"batch": B, "seq_len": T, "heads_q": HQ, "heads_k": HK, "head_dim": D,
+                                 "hidden": HID, "mlp": MLP},
+                      "steps": args.steps, "warmup": args.warmup, "kernels": out}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -452,11 +504,15 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the oracle timing on the host cores")
     ap.add_argument("--batch", type=int, default=CFG["batch"],
                     help="sequences per GPU (default: the workload's 8; smaller only for profiling captures)")
+    ap.add_argument("--component", choices=("attention", "prefill"), default="attention",
+                    help="prefill: time the Llama prefill companion kernels instead (one extra JSON line)")
     args = ap.parse_args()
     CFG["batch"] = args.batch
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
-    if args.impl == "reference":
+    if args.component == "prefill":
+        run_prefill_components(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -205,6 +205,37 @@ int tm_attn_fwd_ex(const tm_attn_params* params, const tm_attn_tuning* tuning, v
  */
 int tm_attn_fwd_noalloc(const tm_attn_params* params, const tm_attn_tuning* tuning, void* stream);
 
+/*
+ * Llama prefill companions (models/tilemix_llama.py:718-895), fp16.
+ *
+ * tm_rotary_token_major replaces rotary_token_major / _rotary (:797-822):
+ * split-half RoPE of q [batch, heads_q, seq_len, head_dim] and k [batch,
+ * heads_k, seq_len, head_dim] (element strides for batch / head / token; the
+ * last dim contiguous, rows 16-byte aligned) with cos / sin [1 or batch,
+ * seq_len, head_dim] (batch stride 0 when broadcast), into token-major oq
+ * [batch, seq_len, heads_q, head_dim] and ok [batch, seq_len, heads_k,
+ * head_dim] (contiguous). head_dim 64 or 128.
+ * If k8 is non-NULL the same pass also quantises the rotated K for the
+ * attention (quant_per_block_varlen.py:6-45, sm_scale 1, blocks of blkk = 64 or
+ * 128 tokens per sequence and KV head): k8 int8 [batch * seq_len, heads_k,
+ * head_dim], optional k_scale_f16 / k_scale_f32 [batch * ceil(seq_len / blkk),
+ * heads_k], bit-identical to tm_quant_per_block_int8 run on ok.
+ */
+int tm_rotary_token_major(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k, int64_t k_sb,
+                          int64_t k_sh, int64_t k_st, const void* cos, int64_t cos_sb, int64_t cos_st,
+                          const void* sin, int64_t sin_sb, int64_t sin_st, int batch, int heads_q, int heads_k,
+                          int seq_len, int head_dim, void* oq, void* ok, int8_t* k8, void* k_scale_f16,
+                          float* k_scale_f32, int blkk, void* stream);
+
+/* out = fp16(fp16(silu(gate)) * up) elementwise over n fp16 values; replaces
+ * silu_mul / _silu_mul (:825-866). */
+int tm_silu_mul(const void* gate, const void* up, void* out, int64_t n, void* stream);
+
+/* RMSNorm of `rows` contiguous fp16 rows of `cols` values: var = mean(x^2) in
+ * fp32, out = fp16(weight * fp16(x * rsqrt(var + eps))); replaces the
+ * squared-mean extension and the tail of PrefillRMSNorm (:718-771). */
+int tm_rms_norm(const void* x, const void* weight, void* out, int64_t rows, int cols, float eps, void* stream);
+
 /* Human-readable text for a TM_* status code. */
 const char* tm_status_string(int status);
 

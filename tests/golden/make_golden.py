@@ -161,6 +161,27 @@ def make_interp(ref_root: str):
         print("attn", name, m, flush=True)
 
 
+def make_prefill(ref_root: str):
+    """The reference's prefill rotary kernel (models/tilemix_llama.py:797-822) under the
+    Triton interpreter; its SiLU kernel calls libdevice exp, which the interpreter cannot run."""
+    os.environ["TRITON_INTERPRET"] = "1"
+    sys.path.insert(0, ref_root)
+    import torch
+    import models.tilemix_llama as ref_llama
+
+    for name, b, hq, hk, t, d, cos_b, seed in [("d64", 2, 3, 1, 40, 64, 1, 31), ("d128_b2", 2, 4, 2, 33, 128, 2, 32)]:
+        g = torch.Generator().manual_seed(seed)
+        q = (torch.randn(b, hq, t, d, generator=g) * 3).half()
+        k = (torch.randn(b, hk, t, d, generator=g) * 3).half()
+        cos = torch.randn(cos_b, t, d, generator=g).half()
+        sin = torch.randn(cos_b, t, d, generator=g).half()
+        oq, ok = ref_llama.rotary_token_major(q, k, cos, sin)
+        np.savez_compressed(HERE / f"interp_rotary_{name}.npz", q=q.numpy(), k=k.numpy(), cos=cos.numpy(),
+                            sin=sin.numpy(), oq=oq.transpose(1, 2).contiguous().numpy(),
+                            ok=ok.transpose(1, 2).contiguous().numpy())
+        print("rotary", name, flush=True)
+
+
 if __name__ == "__main__":
     root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TILEMIX_REFERENCE_ROOT", "")
     if not root or not Path(root).exists():
@@ -170,3 +191,5 @@ if __name__ == "__main__":
         make_maps(root)
     if what in ("all", "interp"):
         make_interp(root)
+    if what in ("all", "prefill"):
+        make_prefill(root)

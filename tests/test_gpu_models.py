@@ -58,6 +58,29 @@ def test_llama_prefill_path_and_cache(cuda_device):
     assert cache.get_seq_length() == 1024
 
 
+def test_llama_prefill_fused_k_quantisation_is_exact(cuda_device):
+    """K quantised inside the RoPE pass gives the same logits, bit for bit, as K quantised by
+    the attention's own quantiser (the codes are identical)."""
+    from tilemix_b200.models.tilemix_llama import (TileMixLlamaAttention, configure_tilemix_attention_pattern,
+                                                   inject_tilemix_into_llama, prepare_llama_prefill)
+
+    dev = cuda_device
+    model = _llama(dev)
+    ids = torch.randint(0, 1000, (2, 1024), generator=torch.Generator().manual_seed(4)).to(dev)
+    inject_tilemix_into_llama(model)
+    configure_tilemix_attention_pattern(model, "sptrans", percentage=0.5)
+    prepare_llama_prefill(model)
+    try:
+        with torch.no_grad():
+            TileMixLlamaAttention.fuse_k_quant = True
+            fused = model(ids).logits
+            TileMixLlamaAttention.fuse_k_quant = False
+            separate = model(ids).logits
+    finally:
+        TileMixLlamaAttention.fuse_k_quant = True
+    assert torch.equal(fused, separate)
+
+
 def test_qwen_prefill_tracks_hf(cuda_device):
     from tilemix_b200.models.tilemix_qwen import configure_tilemix_attention_pattern, inject_tilemix_into_qwen
 

@@ -96,3 +96,14 @@ def test_attention_oracle_matches_interpreter(name):
 def test_attention_flops_formula():
     cu = np.array([0, 4096] + [4096 * i for i in range(2, 9)])
     assert ora.attention_flops(cu, 24, 128) == pytest.approx(8.248e11, rel=1e-3)
+
+
+@pytest.mark.parametrize("name", ["d64", "d128_b2"])
+def test_rotary_oracle_matches_reference(name):
+    """The prefill RoPE restatement equals the reference's Triton kernel (interpreter run)."""
+    from oracle import prefill_oracle as po
+
+    f = np.load(GOLDEN / f"interp_rotary_{name}.npz")
+    oq, ok = po.rotary_token_major(f["q"], f["k"], f["cos"], f["sin"])
+    assert np.array_equal(oq.view(np.uint16), f["oq"].view(np.uint16))
+    assert np.array_equal(ok.view(np.uint16), f["ok"].view(np.uint16))

@@ -76,6 +76,12 @@ SIGNATURES = {
     "tm_attn_fwd_ex": (c_int, [ctypes.POINTER(TmAttnParams), ctypes.POINTER(TmAttnTuning), c_void_p]),
     "tm_attn_fwd_noalloc": (c_int, [ctypes.POINTER(TmAttnParams), ctypes.POINTER(TmAttnTuning), c_void_p]),
     "tm_build_precision_map": (c_int, [ctypes.POINTER(TmMapParams), c_void_p, c_void_p, c_void_p]),
+    "tm_rotary_token_major": (c_int, [c_void_p, c_i64, c_i64, c_i64, c_void_p, c_i64, c_i64, c_i64,
+                                      c_void_p, c_i64, c_i64, c_void_p, c_i64, c_i64, c_int, c_int, c_int,
+                                      c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                      c_void_p]),
+    "tm_silu_mul": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_void_p]),
+    "tm_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, ctypes.c_float, c_void_p]),
     "tm_status_string": (ctypes.c_char_p, [c_int]),
 }
 

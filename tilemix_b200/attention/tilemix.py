@@ -335,7 +335,8 @@ def _quantize_k(k, cu_seqlens_k, max_seqlen_k, BLKK, equal_len: Optional[int] = 
 @torch.no_grad()
 def _attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q, max_seqlens_k, precision_bitmask, *,
                        block_m, block_n, block_n_mask, BLKQ, BLKK, causal, sm_scale, mode: str, scalar_scales,
-                       int8_use_fp16_v, bias=None, equal_len: Optional[int] = None, o=None, threshold=None):
+                       int8_use_fp16_v, bias=None, equal_len: Optional[int] = None, o=None, threshold=None,
+                       k_quant=None):
     mode_code = _routing_mode_code(mode)
     int8_path = mode_code != ROUTING_MODE_FP16
     _check_kernel_support(q, block_m, block_n, BLKK, int8_path, int8_use_fp16_v, bias, max_seqlens_q, max_seqlens_k)
@@ -348,7 +349,15 @@ def _attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q, max_s
     bm = precision_bitmask.to(device=q.device, dtype=torch.uint64).contiguous()
     kw = {}
     if int8_path:
-        k8, sk16, cuks = _quantize_k(k, cu_k, max_seqlens_k, BLKK, equal_len)
+        if k_quant is not None and equal_len is not None and BLKK == 64:
+            # K codes and fp16 block scales already made (by the RoPE pass), blocks of 64 tokens
+            # per equal-length sequence.
+            k8, sk16 = k_quant
+            nblk = (equal_len + BLKK - 1) // BLKK
+            batch = cu_k.numel() - 1
+            cuks = torch.arange(0, (batch + 1) * nblk, nblk, device=k.device, dtype=torch.int32)
+        else:
+            k8, sk16, cuks = _quantize_k(k, cu_k, max_seqlens_k, BLKK, equal_len)
         kw = dict(k8=k8, sk=sk16, cuks=cuks)
         if BLKQ != 128:
             q8, sq, cuq = per_block_int8_single(q, cu_q, max_seqlens_q, BLK=BLKQ, sm_scale=1.0)

@@ -29,11 +29,15 @@ def _env_flag(name: str, default: str = "0") -> bool:
 def tilemix_varlen_attention(q: Tensor, k: Tensor, v: Tensor, block_m: int, block_n: int, *,
                              block_n_mask: Optional[int] = None, causal: bool, scale: float,
                              precision_map_all: Tensor, candidates: list[tuple[int, int]],
-                             flat_lengths: list[int], bias: Optional[Tensor] = None) -> Tensor:
+                             flat_lengths: list[int], bias: Optional[Tensor] = None,
+                             k_quant: Optional[tuple[Tensor, Tensor]] = None) -> Tensor:
     """Routed FP16/INT8 attention of ``[B, H, T, D]`` q/k/v; returns ``[B, Hq, T, D]``.
 
     ``candidates`` and ``flat_lengths`` are accepted for signature parity and
-    unused, as in the reference.
+    unused, as in the reference. ``k_quant`` (no counterpart in the reference):
+    K already quantised per 64-token block, as ``(k8 [B*T, Hk, D] int8,
+    scales [B*ceil(T/64), Hk] fp16)`` from the fused RoPE pass
+    (``rotary_token_major_quant_k``), so K is not read again to quantise it.
     """
     B, Hq, Tq, D = q.shape
     _, Hk, Tk, Dk = k.shape
@@ -83,5 +87,6 @@ def tilemix_varlen_attention(q: Tensor, k: Tensor, v: Tensor, block_m: int, bloc
     out = _attention_forward(Q, K, V, cu_q, cu_k, Tq, Tk, pm, block_m=block_m, block_n=block_n,
                              block_n_mask=block_n_mask, BLKQ=128, BLKK=64, causal=causal, sm_scale=scale,
                              mode=routing_mode, scalar_scales=scalar_scales,
-                             int8_use_fp16_v=_env_flag("TILEMIX_SCORE_ONLY_PV", "1"), bias=bias, equal_len=Tq)
+                             int8_use_fp16_v=_env_flag("TILEMIX_SCORE_ONLY_PV", "1"), bias=bias, equal_len=Tq,
+                             k_quant=k_quant)
     return out.view(B, Tq, Hq, D).permute(0, 2, 1, 3)

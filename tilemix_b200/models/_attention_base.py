@@ -168,8 +168,9 @@ class TileMixAttentionMixin:
         return precision_map
 
     # -- the attention call (models/tilemix_llama.py:505-646)
-    def _tilemix_attention(self, q: Tensor, k: Tensor, v: Tensor, seqlen: int) -> Tensor:
-        """q [B, nh, T, D], k/v [B, nkv, T, D] -> attention output [B, nh, T, D]."""
+    def _tilemix_attention(self, q: Tensor, k: Tensor, v: Tensor, seqlen: int, k_quant=None) -> Tensor:
+        """q [B, nh, T, D], k/v [B, nkv, T, D] -> attention output [B, nh, T, D]. ``k_quant``:
+        K codes and block scales made with the RoPE (see tilemix_varlen_attention)."""
         head_dim = q.shape[-1]
         bucket = self._get_block_config(seqlen)
         block_n_mask = pick_mask_block_n(seqlen, bucket.block_n)
@@ -184,7 +185,8 @@ class TileMixAttentionMixin:
                                f"precision_map={pm.device}")
         return tilemix_varlen_attention(q, k, v, bucket.block_m, bucket.block_n, block_n_mask=block_n_mask,
                                         causal=True, scale=head_dim ** -0.5, precision_map_all=pm,
-                                        candidates=[(bucket.block_m, bucket.block_n)], flat_lengths=[pm.numel()])
+                                        candidates=[(bucket.block_m, bucket.block_n)], flat_lengths=[pm.numel()],
+                                        k_quant=k_quant)
 
 
 def copy_attention_weights(orig, new) -> None:

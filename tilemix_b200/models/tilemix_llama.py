@@ -32,13 +32,16 @@ from tilemix_b200.models._attention_base import (
 
 __all__ = [
     "BucketConfig", "TileMixLlamaAttention", "inject_tilemix_into_llama", "configure_tilemix_attention_pattern",
-    "PrefillCache", "prepare_llama_prefill", "rotary_token_major", "silu_mul", "pick_block_n_for_64",
-    "pick_mask_block_n",
+    "PrefillCache", "prepare_llama_prefill", "prepare_llama_norms", "PrefillRMSNorm", "rotary_token_major",
+    "rotary_token_major_quant_k", "silu_mul", "rms_norm", "pick_block_n_for_64", "pick_mask_block_n",
 ]
 
 
 class TileMixLlamaAttention(TileMixAttentionMixin, LlamaAttention):
     apply_rotary = staticmethod(apply_rotary_pos_emb)
+    # With the prefill RoPE: quantise K for the attention in the RoPE pass (no counterpart in
+    # the reference; the codes are bit-identical to the attention's own quantiser).
+    fuse_k_quant = True
 
     def __init__(self, config, layer_idx: int):
         super().__init__(config, layer_idx=layer_idx)
@@ -64,11 +67,20 @@ class TileMixLlamaAttention(TileMixAttentionMixin, LlamaAttention):
         if position_embeddings is None:
             position_embeddings = self.rotary_emb(q, position_ids)
         cos, sin = (t.to(dev) for t in position_embeddings)
-        q, k = self.apply_rotary(q, k, cos, sin)
+        k_quant = None
+        if self.apply_rotary is rotary_token_major and self.fuse_k_quant:
+            # prefill path: the RoPE pass also quantises K for the attention
+            q, k, k8, ks = rotary_token_major_quant_k(q, k, cos, sin, 64)
+            k_quant = (k8, ks)
+        else:
+            q, k = self.apply_rotary(q, k, cos, sin)
         if past_kv is not None:
+            k_rot = k
             k, v = past_kv.update(k, v, self.layer_idx,
                                   cache_kwargs={"sin": sin, "cos": cos, "cache_position": cache_position})
-        out = self._tilemix_attention(q, k.to(q.dtype), v.to(q.dtype), seqlen)
+            if k is not k_rot:  # the cache returned other keys: quantise them in the attention
+                k_quant = None
+        out = self._tilemix_attention(q, k.to(q.dtype), v.to(q.dtype), seqlen, k_quant=k_quant)
         return self.o_proj(out.transpose(1, 2).reshape(bsz, seqlen, -1)), None
 
 
@@ -100,10 +112,13 @@ class PrefillCache(Cache):
         super().__init__(layer_class_to_replicate=_PrefillDynamicLayer)
 
 
-def rotary_token_major(q: Tensor, k: Tensor, cos: Tensor, sin: Tensor):
-    """Split-half RoPE that writes token-major outputs ([B, T, H, D] storage, returned as
-    [B, H, T, D] views) so the attention's packing is a no-op. Rounds like the reference's
-    prefill rotary (models/tilemix_llama.py:797-822): fp16(x*cos) + fp16(rot(x)*sin) in fp32."""
+def _stream(t: Tensor):
+    import ctypes
+
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _rotary_args(q: Tensor, k: Tensor, cos: Tensor, sin: Tensor):
     b, hq, t, d = q.shape
     hk = k.shape[1]
     if q.dtype != torch.float16 or any(x.dtype != q.dtype for x in (k, cos, sin)):
@@ -112,28 +127,117 @@ def rotary_token_major(q: Tensor, k: Tensor, cos: Tensor, sin: Tensor):
         raise ValueError("incompatible split-half rotary shapes")
     if cos.shape[0] not in (1, b):
         raise ValueError("rotary batch must be one or match the input")
-    c = cos.float()[:, None]
-    s = sin.float()[:, None]
-    sign = torch.cat([-torch.ones(d // 2, device=q.device), torch.ones(d // 2, device=q.device)])
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or cos.stride(-1) != 1 or sin.stride(-1) != 1:
+        raise ValueError("rotary operands must have contiguous head dimensions")
+    if not q.is_cuda:
+        raise RuntimeError("the prefill rotary is a CUDA kernel")
+    return b, hq, hk, t, d
 
-    def rot(x):
-        xr = torch.cat([x[..., d // 2:], x[..., :d // 2]], dim=-1).float()
-        a = (x.float() * c).half().float()
-        bpart = (xr * sign * s).half().float()
-        return (a + bpart).half().transpose(1, 2).contiguous().transpose(1, 2)
 
-    return rot(q), rot(k)
+def _launch_rotary(q, k, cos, sin, oq, ok, k8=None, k_scale=None, blkk=64):
+    import ctypes
+
+    from tilemix_b200._lib import check, lib
+
+    b, hq, hk, t, d = _rotary_args(q, k, cos, sin)
+    cb = cos.stride(0) if cos.shape[0] > 1 else 0
+    sb = sin.stride(0) if sin.shape[0] > 1 else 0
+    ptr = lambda x: ctypes.c_void_p(x.data_ptr() if x is not None else 0)  # noqa: E731
+    with torch.cuda.device(q.device):
+        rc = lib().tm_rotary_token_major(ptr(q), q.stride(0), q.stride(1), q.stride(2), ptr(k), k.stride(0),
+                                         k.stride(1), k.stride(2), ptr(cos), cb, cos.stride(1), ptr(sin), sb,
+                                         sin.stride(1), b, hq, hk, t, d, ptr(oq), ptr(ok), ptr(k8), ptr(k_scale),
+                                         ctypes.c_void_p(0), blkk, _stream(q))
+    check(rc, "tm_rotary_token_major")
+
+
+def rotary_token_major(q: Tensor, k: Tensor, cos: Tensor, sin: Tensor):
+    """Split-half RoPE (models/tilemix_llama.py:797-822) by the library's CUDA kernel. Writes
+    token-major outputs ([B, T, H, D] storage, returned as [B, H, T, D] views) so the
+    attention's packing is a no-op; rounds as the reference: fp16(x*cos) + fp16(rot(x)*sin),
+    the sum formed in fp32."""
+    b, hq, hk, t, d = _rotary_args(q, k, cos, sin)
+    oq = torch.empty((b, t, hq, d), device=q.device, dtype=q.dtype)
+    ok = torch.empty((b, t, hk, d), device=k.device, dtype=k.dtype)
+    _launch_rotary(q, k, cos, sin, oq, ok)
+    return oq.transpose(1, 2), ok.transpose(1, 2)
+
+
+def rotary_token_major_quant_k(q: Tensor, k: Tensor, cos: Tensor, sin: Tensor, blkk: int = 64):
+    """rotary_token_major that also quantises the rotated K per block of ``blkk`` tokens for the
+    attention in the same pass (no counterpart in the reference, which re-reads K in its
+    quantiser). Returns (q_rot, k_rot, k8 [B*T, HK, D] int8, k_scale [B*ceil(T/blkk), HK] fp16)."""
+    b, hq, hk, t, d = _rotary_args(q, k, cos, sin)
+    oq = torch.empty((b, t, hq, d), device=q.device, dtype=q.dtype)
+    ok = torch.empty((b, t, hk, d), device=k.device, dtype=k.dtype)
+    k8 = torch.empty((b * t, hk, d), device=k.device, dtype=torch.int8)
+    ks = torch.empty((b * ((t + blkk - 1) // blkk), hk), device=k.device, dtype=torch.float16)
+    _launch_rotary(q, k, cos, sin, oq, ok, k8, ks, blkk)
+    return oq.transpose(1, 2), ok.transpose(1, 2), k8, ks
 
 
 def silu_mul(gate: Tensor, up: Tensor) -> Tensor:
-    """fp16(silu(gate)) * up in fp32, rounded to fp16 (models/tilemix_llama.py:825-848)."""
+    """fp16(silu(gate)) * up in fp32, rounded to fp16 (models/tilemix_llama.py:825-848), by the
+    library's CUDA kernel."""
+    import ctypes
+
+    from tilemix_b200._lib import check, lib
+
     if gate.dtype != torch.float16 or up.dtype != gate.dtype or gate.shape != up.shape:
         raise ValueError("SiLU requires equally shaped FP16 operands")
     if not gate.is_contiguous() or not up.is_contiguous():
         raise ValueError("SiLU requires contiguous operands")
-    g = gate.float()
-    act = (g / (1.0 + torch.exp(-g))).half()
-    return (act.float() * up.float()).half()
+    if not gate.is_cuda:
+        raise RuntimeError("the prefill SiLU is a CUDA kernel")
+    out = torch.empty_like(gate)
+    with torch.cuda.device(gate.device):
+        rc = lib().tm_silu_mul(ctypes.c_void_p(gate.data_ptr()), ctypes.c_void_p(up.data_ptr()),
+                               ctypes.c_void_p(out.data_ptr()), gate.numel(), _stream(gate))
+    check(rc, "tm_silu_mul")
+    return out
+
+
+def rms_norm(x: Tensor, weight: Tensor, eps: float) -> Tensor:
+    """fp16(weight * fp16(x * rsqrt(mean(x^2) + eps))) over the last dim, the mean in fp32
+    (PrefillRMSNorm, models/tilemix_llama.py:718-771), by the library's CUDA kernel."""
+    import ctypes
+
+    from tilemix_b200._lib import check, lib
+
+    if x.dtype != torch.float16 or weight.dtype != torch.float16 or weight.shape != x.shape[-1:]:
+        raise ValueError("the prefill RMSNorm requires FP16 rows and a matching FP16 weight")
+    if not x.is_cuda:
+        raise RuntimeError("the prefill RMSNorm is a CUDA kernel")
+    xc = x.contiguous()
+    w = weight.contiguous()
+    out = torch.empty_like(xc)
+    with torch.cuda.device(x.device):
+        rc = lib().tm_rms_norm(ctypes.c_void_p(xc.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+                               ctypes.c_void_p(out.data_ptr()), xc.numel() // x.shape[-1], x.shape[-1],
+                               ctypes.c_float(eps), _stream(x))
+    check(rc, "tm_rms_norm")
+    return out
+
+
+class PrefillRMSNorm(nn.Module):
+    """RMSNorm of the prefill path (models/tilemix_llama.py:757-771) on the CUDA kernel."""
+
+    def __init__(self, original):
+        super().__init__()
+        self.weight = original.weight
+        self.variance_epsilon = original.variance_epsilon
+        self.train(original.training)
+
+    def forward(self, hidden_states):
+        return rms_norm(hidden_states, self.weight, self.variance_epsilon)
+
+
+def prepare_llama_norms(model):
+    """Replace every RMSNorm of the decoder with PrefillRMSNorm (models/tilemix_llama.py:774-778)."""
+    for layer in model.model.layers:
+        layer.input_layernorm = PrefillRMSNorm(layer.input_layernorm)
+        layer.post_attention_layernorm = PrefillRMSNorm(layer.post_attention_layernorm)
+    model.model.norm = PrefillRMSNorm(model.model.norm)
 
 
 class PrefillMLP(nn.Module):
@@ -149,8 +253,8 @@ class PrefillMLP(nn.Module):
 
 
 def prepare_llama_prefill(model):
-    """Switch an injected, eval-mode FP16 SiLU Llama to the prefill path: token-major RoPE
-    and the fused SiLU-multiply MLP (models/tilemix_llama.py:883-895). RMSNorm stays HF's."""
+    """Switch an injected, eval-mode FP16 SiLU Llama to the prefill path: the CUDA RMSNorm,
+    token-major RoPE and the fused SiLU-multiply MLP (models/tilemix_llama.py:883-895)."""
     if model.training or model.config.hidden_act != "silu":
         raise ValueError("prefill requires an eval-mode SiLU LLaMA")
     for layer in model.model.layers:
@@ -158,6 +262,7 @@ def prepare_llama_prefill(model):
             raise ValueError("inject TileMix attention before preparing prefill")
         if layer.mlp.gate_proj.weight.dtype != torch.float16:
             raise ValueError("prefill requires FP16 model weights")
+    prepare_llama_norms(model)
     for layer in model.model.layers:
         layer.self_attn.apply_rotary = rotary_token_major
         layer.mlp = PrefillMLP(layer.mlp)
