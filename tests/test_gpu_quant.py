@@ -32,3 +32,23 @@ def test_quant_all_zero_block(cuda_device):
     x8, xs, _ = per_block_int8_single(x.to(cuda_device), cu.to(cuda_device), 128, BLK=128)
     assert float(xs[0, 0]) == 0.0 and int(x8[:, 0].abs().max()) == 0
     assert int(x8[:, 1].min()) == 127
+
+
+@pytest.mark.parametrize("blk,sm_scale", [(64, 1.0), (128, 1.0), (64, 0.5), (256, 1.0)])
+def test_quant_special_values(cuda_device, blk, sm_scale):
+    """A block holding inf quantises to zeros (x / inf is 0, or NaN which truncates to 0), on
+    the unit-scale fast path (64 / 128-token blocks) and on the generic kernel (other scales /
+    blocks). (NaN inputs are left out: the oracle follows the Triton interpreter, whose numpy
+    max propagates NaN into the scale, while GPU max instructions, the reference's included,
+    skip it.)"""
+    from tilemix_b200.attention.quant_per_block_varlen import per_block_int8_single
+
+    q, _, _, cu = make_qkv([300, 200], 2, 1, 128, seed=9, outliers=1)
+    q[70, 1, 3] = float("inf")
+    q[210, 0, 9] = -float("inf")
+    x8, xs, cus = per_block_int8_single(q.to(cuda_device), cu.to(cuda_device), 300, BLK=blk, sm_scale=sm_scale)
+    torch.cuda.synchronize()
+    r8, rs, rcu = ora.per_block_int8_single(q.numpy(), cu.numpy(), 300, BLK=blk, sm_scale=sm_scale)
+    assert np.array_equal(cus.cpu().numpy(), rcu)
+    assert np.array_equal(xs.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(x8.cpu().numpy(), r8)

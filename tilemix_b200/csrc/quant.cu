@@ -123,6 +123,79 @@ __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_kernel(
   }
 }
 
+// The same quantisation for sm_scale == 1, head dims 64 / 128 and blocks of
+// 64 / 128 tokens: the case of every K (and V) the attention quantises. Sizes
+// are compile-time (no per-vector division), the block stays in registers, and
+// the codes come from quant_code_pair_fma: exact here because every |x| of a
+// block is at most its absmax m, an fp16 value, with scale = m / 127 (checked
+// against the reference rounding for all such pairs). A block whose scale is 0
+// or not finite quantises to zeros and a NaN value to 0, as in the reference.
+template <int DIM, int BLK>
+__global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_unit_kernel(
+    const __half* __restrict__ x, int64_t x_stride_tok, int64_t x_stride_head, const int32_t* __restrict__ cu_seqlens,
+    const int32_t* __restrict__ cu_scale, int heads, int8_t* __restrict__ out, int64_t o_stride_tok,
+    int64_t o_stride_head, float* __restrict__ scale_f32, __half* __restrict__ scale_f16) {
+  constexpr int kVecPerRow = DIM / 8;
+  constexpr int kVecs = BLK * kVecPerRow / kQuantThreads;  // 16-byte vectors per thread
+  __shared__ float red[kQuantThreads / 32];
+  const int off_blk = blockIdx.x, off_h = blockIdx.y, off_b = blockIdx.z;
+  const int start = cu_seqlens[off_b];
+  const int len = cu_seqlens[off_b + 1] - start;
+  if (off_blk * BLK >= len) return;
+  const int rows = min(BLK, len - off_blk * BLK);
+  const int64_t tok0 = static_cast<int64_t>(start) + static_cast<int64_t>(off_blk) * BLK;
+  const __half* xb = x + tok0 * x_stride_tok + static_cast<int64_t>(off_h) * x_stride_head;
+  int8_t* ob = out + tok0 * o_stride_tok + static_cast<int64_t>(off_h) * o_stride_head;
+  const int c = (threadIdx.x % kVecPerRow) * 8;
+  uint4 v[kVecs];
+  uint32_t am2 = 0u;
+#pragma unroll
+  for (int i = 0; i < kVecs; ++i) {
+    const int r = i * (kQuantThreads / kVecPerRow) + threadIdx.x / kVecPerRow;
+    v[i] = r < rows ? __ldg(reinterpret_cast<const uint4*>(xb + r * x_stride_tok + c)) : make_uint4(0, 0, 0, 0);
+    uint32_t a, b;
+    asm("max.f16x2 %0, %1, %2;" : "=r"(a) : "r"(v[i].x & 0x7FFF7FFFu), "r"(v[i].y & 0x7FFF7FFFu));
+    asm("max.f16x2 %0, %1, %2;" : "=r"(b) : "r"(v[i].z & 0x7FFF7FFFu), "r"(v[i].w & 0x7FFF7FFFu));
+    asm("max.f16x2 %0, %1, %2;" : "=r"(a) : "r"(a), "r"(b));
+    asm("max.f16x2 %0, %1, %2;" : "=r"(am2) : "r"(am2), "r"(a));
+  }
+  const float2 amf = __half22float2(*reinterpret_cast<const __half2*>(&am2));
+  const float amax = block_absmax_reduce(fmaxf(amf.x, amf.y), red);
+  const float scale = __fdiv_rn(amax, 127.f);
+  const float rscale = __frcp_rn(scale);
+  const bool finite = scale > 0.f && scale <= 3.4028235e38f;
+  uint64_t r2, ns2;
+  r2 = (static_cast<uint64_t>(__float_as_uint(rscale)) << 32) | __float_as_uint(rscale);
+  ns2 = (static_cast<uint64_t>(__float_as_uint(-scale)) << 32) | __float_as_uint(-scale);
+#pragma unroll
+  for (int i = 0; i < kVecs; ++i) {
+    const int r = i * (kQuantThreads / kVecPerRow) + threadIdx.x / kVecPerRow;
+    if (r >= rows) continue;
+    const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
+    uint32_t u[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      if (finite) {
+        quant_code_pair_fma(f.x, f.y, r2, ns2, &u[2 * e], &u[2 * e + 1]);
+        if (f.x != f.x) u[2 * e] = 0u;  // NaN truncates to 0 in the reference
+        if (f.y != f.y) u[2 * e + 1] = 0u;
+      } else {
+        u[2 * e] = 0u;
+        u[2 * e + 1] = 0u;
+      }
+    }
+    const uint32_t lo = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410);
+    const uint32_t hi = __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410);
+    *reinterpret_cast<uint2*>(ob + r * o_stride_tok + c) = make_uint2(lo, hi);
+  }
+  if (threadIdx.x == 0) {
+    const int64_t sidx = (static_cast<int64_t>(cu_scale[off_b]) + off_blk) * heads + off_h;
+    if (scale_f32 != nullptr) scale_f32[sidx] = scale;
+    if (scale_f16 != nullptr) scale_f16[sidx] = __float2half_rn(scale);
+  }
+}
+
 }  // namespace tilemix
 
 extern "C" int tm_quant_per_block_int8(const void* x, int64_t x_stride_tok, int64_t x_stride_head,
@@ -141,7 +214,26 @@ extern "C" int tm_quant_per_block_int8(const void* x, int64_t x_stride_tok, int6
   const int nblk = (max_seqlen + blk - 1) / blk;
   if (heads > 65535 || batch > 65535) return TM_ERR_SHAPE;
   dim3 grid(nblk, heads, batch);
-  tilemix::quant_per_block_int8_kernel<<<grid, tilemix::kQuantThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (sm_scale == 1.0f && (dim == 64 || dim == 128) && (blk == 64 || blk == 128)) {
+    using namespace tilemix;
+    const __half* xh = static_cast<const __half*>(x);
+    __half* s16 = static_cast<__half*>(scale_f16);
+    if (dim == 128 && blk == 64)
+      quant_per_block_int8_unit_kernel<128, 64><<<grid, kQuantThreads, 0, st>>>(
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+    else if (dim == 128)
+      quant_per_block_int8_unit_kernel<128, 128><<<grid, kQuantThreads, 0, st>>>(
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+    else if (blk == 64)
+      quant_per_block_int8_unit_kernel<64, 64><<<grid, kQuantThreads, 0, st>>>(
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+    else
+      quant_per_block_int8_unit_kernel<64, 128><<<grid, kQuantThreads, 0, st>>>(
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+    return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
+  }
+  tilemix::quant_per_block_int8_kernel<<<grid, tilemix::kQuantThreads, 0, st>>>(
       static_cast<const __half*>(x), x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, dim, blk, sm_scale,
       out, out_stride_tok, out_stride_head, scale_f32, static_cast<__half*>(scale_f16));
   const cudaError_t e = cudaGetLastError();
