@@ -117,3 +117,25 @@ def test_attention_bias_matches_oracle(cuda_device, lens, hq, hk, d, block_m, mo
     assert diff.mean() <= MEAN_ABS, float(diff.mean())
     assert diff.max() <= 3e-2, float(diff.max())
     assert int((diff > MAX_ABS).sum()) <= 5e-4 * diff.size, (int((diff > MAX_ABS).sum()), diff.size)
+
+
+@pytest.mark.parametrize("chunk,ring", [(1, 2), (2, 3), (4, 2)])
+def test_from_host_entry_point_matches_device_call(cuda_device, chunk, ring):
+    """Streaming sequences from pinned host memory gives the device call's output bit for bit."""
+    from tilemix_b200.attention.precision_maps import make_precision_bitmask
+    from tilemix_b200.attention.tilemix_varlen import tilemix_varlen_attention, tilemix_varlen_attention_from_host
+
+    B, T, hq, hk, d = 3, 1024, 6, 2, 128
+    q, k, v, _ = make_qkv([T] * B, hq, hk, d, seed=8, outliers=2)
+    dev = cuda_device
+    words = make_precision_bitmask(T, 128, 64, None, 0.5, "sptrans", {"percentage": 0.5}, 64, device=dev)
+    pm = words.view(torch.int64).repeat(hk).view(torch.uint64)
+    ref = tilemix_varlen_attention(*(x.to(dev).view(B, T, -1, d).permute(0, 2, 1, 3) for x in (q, k, v)), 128, 64,
+                                   block_n_mask=64, causal=True, scale=d ** -0.5, precision_map_all=pm,
+                                   candidates=[], flat_lengths=[])
+    out = torch.empty((B * T, hq, d), dtype=torch.float16).pin_memory()
+    tilemix_varlen_attention_from_host(q.pin_memory(), k.pin_memory(), v.pin_memory(), out, T, 128, 64,
+                                       block_n_mask=64, causal=True, scale=d ** -0.5, precision_map_all=pm,
+                                       device=dev, chunk_seqs=chunk, ring=ring)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref.permute(0, 2, 1, 3).reshape(B * T, hq, d).cpu())

@@ -9,7 +9,10 @@ routed attention with the reference's fixed settings (``BLKQ=128``,
 mode from ``TILEMIX_BITMASK_ROUTING_MODE``, FP16 V from
 ``TILEMIX_SCORE_ONLY_PV``). Because every sequence has length T, the K scale
 offsets are computed without a device-to-host read, so the call never
-synchronises the host.
+synchronises the host. ``tilemix_varlen_attention_from_host`` is the same attention
+for packed inputs and output in pinned host memory, streamed through the GPU so
+that the host-device copies of one chunk of sequences overlap the attention of
+another.
 """
 from __future__ import annotations
 
@@ -90,3 +93,99 @@ def tilemix_varlen_attention(q: Tensor, k: Tensor, v: Tensor, block_m: int, bloc
                              int8_use_fp16_v=_env_flag("TILEMIX_SCORE_ONLY_PV", "1"), bias=bias, equal_len=Tq,
                              k_quant=k_quant)
     return out.view(B, Tq, Hq, D).permute(0, 2, 1, 3)
+
+
+@torch.no_grad()
+def tilemix_varlen_attention_from_host(q: Tensor, k: Tensor, v: Tensor, out: Tensor, seq_len: int, block_m: int,
+                                       block_n: int, *, block_n_mask: Optional[int] = None, causal: bool,
+                                       scale: float, precision_map_all: Tensor,
+                                       device: Optional[torch.device] = None, chunk_seqs: int = 1,
+                                       ring: int = 2) -> Tensor:
+    """``tilemix_varlen_attention`` for inputs and output in pinned host memory (no counterpart
+    in the reference, whose entry points take device tensors).
+
+    ``q`` ``[B*T, Hq, D]``, ``k`` / ``v`` ``[B*T, Hk, D]`` and ``out`` ``[B*T, Hq, D]`` are
+    token-major packed fp16 CPU tensors in pinned memory, ``T = seq_len`` for every sequence.
+    Sequences are streamed through the GPU ``chunk_seqs`` at a time: the copy of chunk c+1
+    to the device, the attention of chunk c and the copy of chunk c-1 back to ``out`` run on
+    three streams and overlap (PCIe moves both directions at once), with ``ring`` device
+    buffers per tensor. Each chunk is an independent call of the same attention, so ``out``
+    is bit-identical to the device call on the whole batch. Asynchronous on the current
+    stream of ``device`` (default: the current CUDA device): work issued there afterwards
+    (or an event recorded there) comes after the last copy back. Returns ``out``.
+    """
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+        if t.is_cuda or not t.is_pinned():
+            raise ValueError(f"{name} must be a pinned host tensor")
+        if t.dtype != torch.float16 or t.ndim != 3 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous fp16 [tokens, heads, dim] tensor")
+    total, Hq, D = q.shape
+    T = int(seq_len)
+    if T <= 0 or total % T:
+        raise ValueError("the token count must be a multiple of seq_len")
+    B = total // T
+    Hk = k.shape[1]
+    if k.shape != (total, Hk, D) or v.shape != k.shape or out.shape != q.shape:
+        raise ValueError("q / k / v / out shapes do not match")
+    if chunk_seqs <= 0 or ring <= 0:
+        raise ValueError("chunk_seqs and ring must be positive")
+    if block_n_mask is None:
+        block_n_mask = block_n
+    routing_mode = (os.getenv("TILEMIX_BITMASK_ROUTING_MODE") or "mixed").strip().lower()
+    if routing_mode == "auto":
+        from tilemix_b200.attention.tilemix import classify_bitmask_routing
+        routing_mode = classify_bitmask_routing(precision_map_all, seqlen_q=T, seqlen_k=T, block_m=block_m,
+                                                block_n=block_n, block_n_mask=block_n_mask, causal=causal)
+    _routing_mode_code(routing_mode)
+    scalar_scales = block_m == 128 and block_n == 64
+    pm = precision_map_all.to(device=dev, dtype=torch.uint64).contiguous()
+    with torch.cuda.device(dev):
+        main = torch.cuda.current_stream(dev)
+        s_in, s_run, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+        for s in (s_in, s_run, s_out):
+            s.wait_stream(main)  # the host buffers / map are ready as of the caller's stream
+        cs = min(chunk_seqs, B)
+        rows = cs * T
+        slots = [dict(q=torch.empty((rows, Hq, D), device=dev, dtype=q.dtype),
+                      k=torch.empty((rows, Hk, D), device=dev, dtype=k.dtype),
+                      v=torch.empty((rows, Hk, D), device=dev, dtype=v.dtype),
+                      o=torch.empty((rows, Hq, D), device=dev, dtype=q.dtype),
+                      free_in=None, free_out=None) for _ in range(min(ring, (B + cs - 1) // cs))]
+        fp16_v = _env_flag("TILEMIX_SCORE_ONLY_PV", "1")
+        for c, b0 in enumerate(range(0, B, cs)):
+            nb = min(cs, B - b0)
+            r0, r1 = b0 * T, (b0 + nb) * T
+            sl = slots[c % len(slots)]
+            with torch.cuda.stream(s_in):
+                if sl["free_in"] is not None:
+                    s_in.wait_event(sl["free_in"])  # the previous chunk in this slot has been computed
+                n = r1 - r0
+                sl["q"][:n].copy_(q[r0:r1], non_blocking=True)
+                sl["k"][:n].copy_(k[r0:r1], non_blocking=True)
+                sl["v"][:n].copy_(v[r0:r1], non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(s_in)
+            with torch.cuda.stream(s_run):
+                s_run.wait_event(ready)
+                if sl["free_out"] is not None:
+                    s_run.wait_event(sl["free_out"])  # the previous chunk's output has been copied out
+                cu = torch.arange(0, (nb + 1) * T, T, device=dev, dtype=torch.int32)
+                _attention_forward(sl["q"][:n], sl["k"][:n], sl["v"][:n], cu, cu, T, T, pm, block_m=block_m,
+                                   block_n=block_n, block_n_mask=block_n_mask, BLKQ=128, BLKK=64, causal=causal,
+                                   sm_scale=scale, mode=routing_mode, scalar_scales=scalar_scales,
+                                   int8_use_fp16_v=fp16_v, equal_len=T, o=sl["o"][:n])
+                done = torch.cuda.Event()
+                done.record(s_run)
+                sl["free_in"] = done
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                out[r0:r1].copy_(sl["o"][:n], non_blocking=True)
+                copied = torch.cuda.Event()
+                copied.record(s_out)
+                sl["free_out"] = copied
+        for s in (s_in, s_run, s_out):
+            main.wait_stream(s)
+        # The ring buffers were allocated on the caller's stream, which now waits for all three
+        # streams: their memory is reused only by work ordered after these copies.
+    return out
