@@ -21,7 +21,7 @@ NAMES = ["cfg1_sptrans", "cfg1_zero", "cfg1_one", "gqa128_sptrans", "gqa128_bigb
 
 
 @pytest.mark.parametrize("name", NAMES)
-@pytest.mark.parametrize("threshold", ["0", "8"])
+@pytest.mark.parametrize("threshold", ["0", "8", "15"])
 def test_attention_matches_reference_fixture(cuda_device, monkeypatch, name, threshold):
     from tilemix_b200.attention.tilemix import device_error_code, tilemix_attention_with_quant
 
