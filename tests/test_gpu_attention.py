@@ -54,6 +54,9 @@ CASES = [
     ([1024], 3, 1, 128, 128, 64, "int8"),
     ([300, 700, 129], 4, 2, 128, 128, 128, "mixed"),  # varlen, mask group of 2 tiles
     ([777, 64, 513], 2, 1, 64, 64, 64, "mixed"),
+    ([896, 333], 3, 1, 128, 128, 64, "mixed"),    # GQA group 3, 21 tiles: one item holds a single tile
+    ([640, 200], 5, 5, 128, 128, 64, "mixed"),    # MHA (group 1): items of consecutive query blocks
+    ([520], 8, 2, 128, 128, 64, "mixed"),         # group 4: two head pairs per query block
 ]
 
 

@@ -38,7 +38,7 @@ struct AttnArgs {
   int HQ, HK, group, D;
   int block_m, block_n_mask, blkq, blkk;
   int causal, mode, fuse_q;
-  int pair_heads;  // paired kernel: 1 = CTA holds two heads of one KV group, 0 = two m-tiles of one head
+  int pair_heads;  // paired128 / split kernels: 1 = CTA holds two heads of one KV group, 0 = two m-tiles of one head
   int o_vec32;     // O rows start on 32-byte boundaries (out 32-byte aligned, strides multiples of 16)
   float qk_scale;
   float rescale_threshold;

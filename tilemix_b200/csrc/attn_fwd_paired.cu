@@ -4,9 +4,12 @@
 //
 // Same semantics as the general kernel (attention/triton/tilemix.py:503-951);
 // different mapping. A work item is two 128-row query tiles X = A, B that share
-// a KV head: either two Q heads of one GQA group at the same query block (their
-// routing words are the same map row), or two consecutive query blocks of one
-// head. Every K/V tile is loaded once into shared memory and feeds both tiles.
+// a KV head. The tiles of one (sequence, KV head) unit, group x query blocks of
+// them, are listed by query block (last first), then Q head, and consecutive
+// tiles form the items: two heads of one GQA group at the same query block
+// (equal key loops) wherever the group allows, else the last head of a block
+// with the first of the next block down (two key tiles apart). Every K/V tile is
+// loaded once into shared memory and feeds both tiles.
 //
 // Persistent: one CTA per SM walks a static list of work items, longest first
 // (the last query blocks under causal masking), dealt out in snake order
@@ -92,8 +95,8 @@ struct QTile {
 };
 
 // One work item, resolved from its index. Items are ordered by level x (0 =
-// the last query block pair, the longest under causal masking), then sequence,
-// then head slot.
+// the first pair of each unit's tile list, the longest under causal masking),
+// then sequence, then KV head.
 struct Item {
   QTile tl[2];
   int q_start, seqlen_q, k_start, seqlen_k;
@@ -103,6 +106,7 @@ struct Item {
 
 struct Grid {
   int nx, ny, nz, n_items;
+  int mt;  // query blocks of the longest sequence
 };
 
 __device__ __forceinline__ Item load_item(int it, const AttnArgs& a, const Grid& g) {
@@ -120,23 +124,22 @@ __device__ __forceinline__ Item load_item(int it, const AttnArgs& a, const Grid&
   m.ks_base = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[z] : 0;
   m.ks_end = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[z + 1] : 0;
   const int m_blocks = (m.seqlen_q + kRows - 1) / kRows;
-  const int rev = g.nx - 1 - x;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    if (a.pair_heads) {
-      m.tl[t].hq = 2 * y + t;
-      m.tl[t].mtile = rev;
-    } else {
-      m.tl[t].hq = y;
-      m.tl[t].mtile = 2 * rev + t;
-    }
+    // Tile f of the unit's list: query block g.mt-1 - f/group, head f%group of
+    // the KV head's group. Past the end of the list (group * g.mt odd) the
+    // slot is absent: its block lies beyond every sequence.
+    const int f = 2 * x + t;
+    const int fb = f / a.group;
+    m.tl[t].hq = y * a.group + (f - fb * a.group);
+    m.tl[t].mtile = fb < g.mt ? g.mt - 1 - fb : g.mt;
     const bool valid = m.tl[t].mtile * kRows < m.seqlen_q;
     m.tl[t].nb = valid ? visited_key_tiles(m.tl[t].mtile * kRows, kRows, m.seqlen_q, m.seqlen_k, a.causal) : 0;
     m.tl[t].bits = 0;
     if (valid && a.mode == TM_ROUTE_MIXED)
       m.tl[t].bits = a.bitmask[static_cast<int64_t>(m.tl[t].hq / a.group) * m_blocks + m.tl[t].mtile];
   }
-  m.hk = m.tl[0].hq / a.group;  // both tiles share the KV head
+  m.hk = y;  // both tiles share the KV head
   m.n_iter = max(m.tl[0].nb, m.tl[1].nb);
   return m;
 }
@@ -700,13 +703,9 @@ int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUten
   }
   const int mtiles = (max_seqlen_q + kRows - 1) / kRows;
   Grid g;
-  if (a.pair_heads) {
-    g.nx = mtiles;
-    g.ny = a.HQ / 2;
-  } else {
-    g.nx = (mtiles + 1) / 2;
-    g.ny = a.HQ;
-  }
+  g.mt = mtiles;
+  g.nx = static_cast<int>((static_cast<int64_t>(a.group) * mtiles + 1) / 2);
+  g.ny = a.HK;
   g.nz = batch;
   const int64_t items = static_cast<int64_t>(g.nx) * g.ny * g.nz;
   if (items <= 0) return TM_OK;
