@@ -55,7 +55,7 @@ class TileMixqwenAttention(TileMixAttentionMixin, Qwen2Attention):
         if seqlen < 16:
             return Qwen2Attention.forward(self, hidden_states, position_embeddings, attention_mask,
                                           past_key_values=past_kv, cache_position=cache_position, **kwargs)
-        head_dim = self.config.hidden_size // self.nh
+        head_dim = self.head_dim
         dev = hidden_states.device
         q = self.q_proj(hidden_states).view(bsz, seqlen, self.nh, head_dim).transpose(1, 2)
         k = self.k_proj(hidden_states).view(bsz, seqlen, self.nkv, head_dim).transpose(1, 2)
