@@ -493,28 +493,40 @@ LLAMA_3B = dict(hidden_size=3072, intermediate_size=8192, num_hidden_layers=28, 
                 num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-5, rope_theta=500000.0, vocab_size=128256,
                 tie_word_embeddings=True, max_position_embeddings=8192, initializer_range=0.02,
                 hidden_act="silu")
-PREFILL_A100_MS = 1071.0  # the reference paper's 30.59 K tok/s at B=8, L=4K on an A100 (derived)
+QWEN2_7B = dict(hidden_size=3584, intermediate_size=18944, num_hidden_layers=28, num_attention_heads=28,
+                num_key_value_heads=4, rms_norm_eps=1e-6, rope_theta=1000000.0, vocab_size=152064,
+                tie_word_embeddings=False, max_position_embeddings=32768, initializer_range=0.02,
+                hidden_act="silu")
+# name: (config 3 / 4 of the headline benchmark) architecture, batch, tokens, patterns, A100 ms or None
+MODEL_SPECS = {
+    "llama3b": dict(label="Llama-3.2-3B", config=3, arch=LLAMA_3B, batch=8, seq_len=4096, patterns=("sptrans",),
+                    a100_ms=1071.0,  # the reference paper's 30.59 K tok/s at B=8, L=4K on an A100 (derived)
+                    a100_note="vs_baseline = ms / 1071 ms, the A100 40GB figure derived from the reference paper"),
+    "qwen7b": dict(label="Qwen2-7B", config=4, arch=QWEN2_7B, batch=4, seq_len=16384, patterns=("band", "bigbird"),
+                   a100_ms=None, a100_note="the reference publishes no Qwen2-7B number beyond 4K tokens"),
+}
 
 
 def run_model_prefill(args) -> None:
-    """--component model: Llama-3.2-3B prefill (config 3) through the public model API:
-    random-init weights (seed 0, std 0.02, fp16), inject_tilemix_into_llama + sptrans 50% +
-    prepare_llama_prefill, 8 x 4096 uniform token ids, PrefillCache and last-position logits.
-    Under torchrun the layers are head-sharded across the N ranks (TP N, one NCCL all-reduce
-    after each attention and MLP block). Each of the timed prefills is bracketed by a barrier
-    and a synchronize; the line reports the median over prefills of the slowest rank's time,
-    as the reference's prefill benchmark takes the median."""
+    """--component model: whole-model prefill through the public model API (config 3:
+    Llama-3.2-3B, 8 x 4096 tokens, sptrans 50 %; ``--model qwen7b``, config 4: Qwen2-7B,
+    4 x 16384 tokens, band and bigbird at 50 %): random-init weights (seed 0, std 0.02, fp16),
+    TileMix attention injected and the routing pattern configured (Llama also
+    prepare_llama_prefill), uniform token ids, PrefillCache and last-position logits. Under
+    torchrun the layers are head-sharded across the N ranks (TP N, one NCCL all-reduce after
+    each attention and MLP block). Each timed prefill is bracketed by a barrier and a
+    synchronize; a line per pattern reports the median over prefills of the slowest rank's
+    time, as the reference's prefill benchmark takes the median."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     import torch
     import torch.distributed as dist
-    from transformers import LlamaConfig, LlamaForCausalLM
 
     from tilemix_b200.models.tensor_parallel import shard_model_for_tensor_parallel
-    from tilemix_b200.models.tilemix_llama import (PrefillCache, configure_tilemix_attention_pattern,
-                                                   inject_tilemix_into_llama, prepare_llama_prefill)
+    from tilemix_b200.models.tilemix_llama import PrefillCache
 
+    spec = MODEL_SPECS[args.model]
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
@@ -525,15 +537,27 @@ def run_model_prefill(args) -> None:
             dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize()
 
-    B, T = CFG["batch"], CFG["seq_len"]
-    cfg = LlamaConfig(**LLAMA_3B)
+    if args.model == "llama3b":
+        from transformers import LlamaConfig as Config, LlamaForCausalLM as Model
+
+        from tilemix_b200.models.tilemix_llama import configure_tilemix_attention_pattern as configure
+        from tilemix_b200.models.tilemix_llama import inject_tilemix_into_llama as inject
+        from tilemix_b200.models.tilemix_llama import prepare_llama_prefill as prepare
+    else:
+        from transformers import Qwen2Config as Config, Qwen2ForCausalLM as Model
+
+        from tilemix_b200.models.tilemix_qwen import configure_tilemix_attention_pattern as configure
+        from tilemix_b200.models.tilemix_qwen import inject_tilemix_into_qwen as inject
+        prepare = None
+    B, T = spec["batch"], spec["seq_len"]
+    cfg = Config(**spec["arch"])
     torch.manual_seed(0)
     with torch.device(dev):
-        model = LlamaForCausalLM(cfg)
+        model = Model(cfg)
     model = model.half().eval()
-    inject_tilemix_into_llama(model)
-    configure_tilemix_attention_pattern(model, "sptrans", percentage=CFG["percentage"])
-    prepare_llama_prefill(model)
+    inject(model)
+    if prepare is not None:
+        prepare(model)
     if world > 1:
         shard_model_for_tensor_parallel(model, rank, world)
     torch.cuda.empty_cache()
@@ -546,60 +570,63 @@ def run_model_prefill(args) -> None:
 
     ids = ids_host.to(dev)
     steps, warmup = max(5, min(args.steps, 20)), max(3, min(args.warmup, 5))
-    for _ in range(warmup):
-        prefill(ids)
-    barrier()
-    sampler = ClockSampler(gpu_id_for(local_rank))
-    sampler.start()
-    times, t_host0 = [], time.time()
-    for _ in range(steps):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for pattern in spec["patterns"]:
+        configure(model, pattern, percentage=0.5)
+        for _ in range(warmup):
+            prefill(ids)
         barrier()
-        e0.record()
-        prefill(ids)
-        e1.record()
-        barrier()
-        times.append(e0.elapsed_time(e1))
-    # end to end: token ids from pinned host memory in, last-position logits back, per prefill
-    e2e_times = []
-    for _ in range(max(3, steps // 2)):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        e0.record()
-        logits_host.copy_(prefill(ids_host.to(dev, non_blocking=True)), non_blocking=True)
-        e1.record()
-        barrier()
-        e2e_times.append(e0.elapsed_time(e1))
-    t_host1 = time.time()
-    sampler.mark(t_host0, t_host1)
-    clocks = sampler.stop()
-    if world > 1:
-        t = torch.tensor([times, e2e_times[:len(times)] + [0.0] * (len(times) - len(e2e_times))],
-                         dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        times = t[0].tolist()
-        e2e_times = t[1, :len(e2e_times)].tolist()
-    ms = statistics.median(times)
-    e2e_ms = statistics.median(e2e_times)
-    tokens = B * T
-    if rank == 0:
-        print(json.dumps({
-            "metric": "Llama-3.2-3B prefill ms (config 3)", "value": ms, "unit": "ms", "n_gpus": world,
-            "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": False,
-            "scaling": "strong", "vs_baseline": ms / PREFILL_A100_MS, "dtype": "fp16+int8",
-            "data": "synthetic (random-init weights seed 0 std 0.02, uniform token ids seed 0)",
-            "config": {"workload": "config 3: Llama-3.2-3B architecture, prefill 8 x 4096 tokens with KV cache "
-                                   "and last-position logits, sptrans 50% INT8",
-                       "model": "Llama-3.2-3B (random init)", "global_batch": B, "seq_len": T,
-                       "parallelism": f"tp{world}" + (": heads and MLP columns sharded, NCCL all-reduce after "
-                                                      "o_proj and down_proj" if world > 1 else ""),
-                       "l2": "every prefill moves the full weights (6.4 GB) and activations, far above L2"},
-            "tokens_per_s": tokens / (ms * 1e-3), "ms_all": times,
-            "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(),
-                    "d2h_bytes_per_step": logits_host.numel() * logits_host.element_size()},
-            "baseline_note": "vs_baseline = ms / 1071 ms, the A100 40GB figure derived from the reference paper",
-            "clocks": clocks,
-        }), flush=True)
+        sampler = ClockSampler(gpu_id_for(local_rank))
+        sampler.start()
+        times, t_host0 = [], time.time()
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
+            e0.record()
+            prefill(ids)
+            e1.record()
+            barrier()
+            times.append(e0.elapsed_time(e1))
+        # end to end: token ids from pinned host memory in, last-position logits back, per prefill
+        e2e_times = []
+        for _ in range(max(3, steps // 2)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
+            e0.record()
+            logits_host.copy_(prefill(ids_host.to(dev, non_blocking=True)), non_blocking=True)
+            e1.record()
+            barrier()
+            e2e_times.append(e0.elapsed_time(e1))
+        t_host1 = time.time()
+        sampler.mark(t_host0, t_host1)
+        clocks = sampler.stop()
+        if world > 1:
+            t = torch.tensor([times, e2e_times + [0.0] * (len(times) - len(e2e_times))], dtype=torch.float64,
+                             device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            times = t[0].tolist()
+            e2e_times = t[1, :len(e2e_times)].tolist()
+        ms = statistics.median(times)
+        e2e_ms = statistics.median(e2e_times)
+        if rank == 0:
+            a100 = spec["a100_ms"]
+            print(json.dumps({
+                "metric": f"{spec['label']} prefill ms (config {spec['config']})", "value": ms, "unit": "ms",
+                "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": (ms / a100) if a100 else None, "dtype": "fp16+int8",
+                "data": "synthetic (random-init weights seed 0 std 0.02, uniform token ids seed 0)",
+                "config": {"workload": f"config {spec['config']}: {spec['label']} architecture, prefill {B} x {T} "
+                                       f"tokens with KV cache and last-position logits, {pattern} 50% INT8",
+                           "model": f"{spec['label']} (random init)", "global_batch": B, "seq_len": T,
+                           "pattern": pattern,
+                           "parallelism": f"tp{world}" + (": heads and MLP columns sharded, NCCL all-reduce "
+                                                          "after o_proj and down_proj" if world > 1 else ""),
+                           "l2": "every prefill moves the full weights and activations, far above L2"},
+                "tokens_per_s": B * T / (ms * 1e-3), "ms_all": times,
+                "e2e": {"value": e2e_ms, "unit": "ms",
+                        "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(),
+                        "d2h_bytes_per_step": logits_host.numel() * logits_host.element_size()},
+                "baseline_note": spec["a100_note"], "clocks": clocks,
+            }), flush=True)
     del model
     if world > 1:
         dist.barrier(device_ids=[local_rank])
@@ -615,6 +642,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the oracle timing on the host cores")
     ap.add_argument("--batch", type=int, default=CFG["batch"],
                     help="sequences per GPU (default: the workload's 8; smaller only for profiling captures)")
+    ap.add_argument("--model", choices=tuple(MODEL_SPECS), default="llama3b",
+                    help="--component model: llama3b (config 3) or qwen7b (config 4)")
     ap.add_argument("--component", choices=("attention", "prefill", "model"), default="attention",
                     help="prefill: time the Llama prefill companion kernels instead; model: Llama-3.2-3B prefill "
                          "ms through the model API (tensor-parallel over the ranks under torchrun)")

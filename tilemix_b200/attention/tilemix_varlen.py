@@ -95,6 +95,20 @@ def tilemix_varlen_attention(q: Tensor, k: Tensor, v: Tensor, block_m: int, bloc
     return out.view(B, Tq, Hq, D).permute(0, 2, 1, 3)
 
 
+# The three streams of the host-resident entry point, one set per device and kept for the
+# process: torch hands out a different pool stream for every new Stream(), and the caching
+# allocator keeps freed blocks per stream, so fresh streams on every call would send each
+# call's scratch allocations to cudaMalloc (which synchronises the device).
+_HOST_STREAMS: dict = {}
+
+
+def _host_streams(dev: torch.device):
+    st = _HOST_STREAMS.get(dev.index)
+    if st is None:
+        st = _HOST_STREAMS[dev.index] = tuple(torch.cuda.Stream(dev) for _ in range(3))
+    return st
+
+
 @torch.no_grad()
 def tilemix_varlen_attention_from_host(q: Tensor, k: Tensor, v: Tensor, out: Tensor, seq_len: int, block_m: int,
                                        block_n: int, *, block_n_mask: Optional[int] = None, causal: bool,
@@ -115,6 +129,10 @@ def tilemix_varlen_attention_from_host(q: Tensor, k: Tensor, v: Tensor, out: Ten
     (or an event recorded there) comes after the last copy back. Returns ``out``.
     """
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if dev.type != "cuda":
+        raise ValueError("device must be a CUDA device")
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
     for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
         if t.is_cuda or not t.is_pinned():
             raise ValueError(f"{name} must be a pinned host tensor")
@@ -142,7 +160,7 @@ def tilemix_varlen_attention_from_host(q: Tensor, k: Tensor, v: Tensor, out: Ten
     pm = precision_map_all.to(device=dev, dtype=torch.uint64).contiguous()
     with torch.cuda.device(dev):
         main = torch.cuda.current_stream(dev)
-        s_in, s_run, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+        s_in, s_run, s_out = _host_streams(dev)
         for s in (s_in, s_run, s_out):
             s.wait_stream(main)  # the host buffers / map are ready as of the caller's stream
         cs = min(chunk_seqs, B)
