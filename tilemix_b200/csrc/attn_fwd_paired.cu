@@ -244,7 +244,7 @@ __device__ __forceinline__ __half transform_q(uint8_t* smem, Barriers* bars, con
   const bool finite = scale > 0.f && scale <= 3.4028235e38f;
   const uint64_t r2 = f32x2_pack(rscale, rscale), ns2 = f32x2_pack(-scale, -scale);
   uint8_t* q8 = smem + kOffQ8 + x * kQ8Bytes;
-#pragma unroll 2
+#pragma unroll 4
   for (int g = 0; g < 8; ++g) {
     // 16 codes of dims [16g, 16g+16) = chunks 2g and 2g+1
     const uint4 ra = *chunk(2 * g), rb = *chunk(2 * g + 1);
@@ -273,33 +273,38 @@ __device__ __forceinline__ __half transform_q(uint8_t* smem, Barriers* bars, con
   return __float2half_rn(scale);
 }
 
-// Write this thread's O row (128 fp32 columns in TMEM) as fp16 O / l, 16
-// columns at a time, and release the accumulator (o_free) once all of it has
-// been read. acc / l: reciprocal once per row, then per element one residual
-// correction (Markstein's method: q0 = a*r, e = a - q0*l, q = q0 + e*r), which
-// gives the correctly rounded quotient for these normal operands. Each thread
-// writes its own row (rows are a token stride apart), 32 bytes per store where
-// the layout allows.
+// Write this thread's O row (128 fp32 columns in TMEM) as fp16 O / l: 32
+// columns per TMEM load (four load / wait round trips), stored 16 at a time,
+// and release the accumulator (o_free) once all of it has been read. acc / l:
+// reciprocal once per row, then per element one residual correction
+// (Markstein's method: q0 = a*r, e = a - q0*l, q = q0 + e*r), which gives the
+// correctly rounded quotient for these normal operands. Each thread writes its
+// own row (rows are a token stride apart), 32 bytes per store where the layout
+// allows.
 __device__ __forceinline__ void epilogue_o_row(uint32_t taddr, bool have_o, float l, __half* orow, bool store,
                                                bool vec32, uint64_t* o_free) {
   const float rl = __frcp_rn(l);
   const uint64_t rl2 = f32x2_pack(rl, rl), nl2 = f32x2_pack(-l, -l);
   uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll 1
-  for (int c = 0; c < 8; ++c) {
-    uint32_t o[16];
+  for (int c32 = 0; c32 < 4; ++c32) {
+    uint32_t o32[32];
     if (have_o) {
-      tmem_ld16(taddr + 16 * c, o);
+      tmem_ld32(taddr + 32 * c32, o32);
       tmem_wait_ld();
     } else {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) o[i] = 0u;
+      for (int i = 0; i < 32; ++i) o32[i] = 0u;
     }
-    if (c == 7) {
+    if (c32 == 3) {
       tc_fence_before();
       mbar_arrive(o_free);
     }
-    if (store) {
+    if (!store) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = 2 * c32 + h;  // 16-column chunk of the row
+      const uint32_t* o = o32 + 16 * h;
       uint32_t w[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
