@@ -633,6 +633,117 @@ def run_model_prefill(args) -> None:
         dist.destroy_process_group()
 
 
+VARLEN = dict(sequences=8, min_len=8192, max_len=131072, heads_q=32, heads_k=8, head_dim=128)
+VARLEN_CASES = (("sptrans", 0.5), ("band", 0.5), ("bigbird", 0.5), ("row_rand", 0.25), ("global", 0.75),
+                ("zero", None), ("one", None))
+
+
+def run_varlen(args) -> None:
+    """--component varlen: config 5, the long-context varlen attention op. 8 sequences of
+    lengths uniform in [8K, 128K] (torch.randint, seed 1), 32 q / 8 kv heads, head_dim 128,
+    fp16 N(0, 1), causal, tiles (128, 64) with the mask-group width the model picks for the
+    longest sequence; one line per routing case (pattern, INT8 share). A step is K
+    quantisation + the attention over the whole batch. Under torchrun the (sequence x KV-head)
+    units are dealt to the ranks longest-processing-time first (tilemix_b200/sharding.py) and
+    packed before the timed region, in groups that read the same routing words, so every
+    rank's results equal the unsharded call's; value = all ranks' FLOPs / slowest rank's
+    time (strong scaling)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    import torch.distributed as dist
+
+    from tilemix_b200.attention import tilemix as tmx
+    from tilemix_b200.attention.precision_maps import make_precision_bitmask
+    from tilemix_b200.models._attention_base import pick_mask_block_n
+    from tilemix_b200.sharding import map_rows, pack_units, plan_units
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=_dt.timedelta(seconds=300), device_id=dev)
+    c = VARLEN
+    lens = torch.randint(c["min_len"], c["max_len"] + 1, (c["sequences"],),
+                         generator=torch.Generator().manual_seed(1)).tolist()
+    cu_list = [0]
+    for n in lens:
+        cu_list.append(cu_list[-1] + n)
+    T_max, HQ, HK, D = max(lens), c["heads_q"], c["heads_k"], c["head_dim"]
+    group = HQ // HK
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn((cu_list[-1], HQ, D), device=dev, generator=g, dtype=torch.float16)
+    k = torch.randn((cu_list[-1], HK, D), device=dev, generator=g, dtype=torch.float16)
+    v = torch.randn((cu_list[-1], HK, D), device=dev, generator=g, dtype=torch.float16)
+    bm, bn = 128, 64
+    bnm = pick_mask_block_n(T_max, bn)
+    flops = float(sum(4 * D * HQ * n * (n + 1) // 2 for n in lens))
+    units = plan_units(lens, HK, world, group)[rank]
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    results = []
+    for pattern, pct in VARLEN_CASES:
+        words = make_precision_bitmask(T_max, bm, bnm, None, pct, pattern,
+                                       {"percentage": pct} if pct is not None else {}, bn, device=dev)
+        pm = words.view(torch.int64).repeat(HK).view(torch.uint64)
+        if world == 1:
+            cu = torch.tensor(cu_list, dtype=torch.int32, device=dev)
+            problems = [(q, k, v, cu, T_max, pm)]
+        else:
+            by_rows: dict = {}
+            for u in units:
+                off, _ = map_rows(pm, u, lens[u[0]], bm)
+                by_rows.setdefault(off, []).append(u)
+            problems = []
+            for off, us in sorted(by_rows.items()):
+                q_r, k_r, v_r, cu_r, mx = pack_units(q, k, v, cu_list, us)
+                problems.append((q_r, k_r, v_r, cu_r, mx, pm[off:off + (mx + bm - 1) // bm].contiguous()))
+
+        def step():
+            for q_, k_, v_, cu_, mx_, pm_ in problems:
+                tmx._attention_forward(q_, k_, v_, cu_, cu_, mx_, mx_, pm_, block_m=bm, block_n=bn, block_n_mask=bnm,
+                                       BLKQ=128, BLKK=64, causal=True, sm_scale=None, mode="mixed",
+                                       scalar_scales=True, int8_use_fp16_v=True)
+
+        for _ in range(2):
+            step()
+        barrier()
+        steps = max(3, min(args.steps, 5))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        barrier()
+        ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        if tmx.device_error_code(dev) != 0:
+            raise RuntimeError("attention kernel reported a device-side timeout")
+        results.append({"pattern": pattern, "int8_percentage": pct, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+                        "launches_per_step": len(problems)})
+        del problems
+    if rank == 0:
+        print(json.dumps({
+            "component": "varlen attention (config 5)", "unit": "TFLOP/s", "n_gpus": world,
+            "scaling": "strong", "dtype": "fp16+int8", "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": "config 5: 8 packed sequences, lengths uniform in [8K, 128K] (seed 1), "
+                                   "32 q / 8 kv heads, head_dim 128, causal", "lengths": lens,
+                       "tokens": cu_list[-1], "block_m": bm, "block_n": bn, "block_n_mask": bnm,
+                       "parallelism": f"shard{world}: (sequence x KV-head) units dealt longest first, no collective"},
+            "flops_per_step": flops, "steps": max(3, min(args.steps, 5)), "warmup": 2, "cases": results,
+        }), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -644,9 +755,10 @@ def main() -> None:
                     help="sequences per GPU (default: the workload's 8; smaller only for profiling captures)")
     ap.add_argument("--model", choices=tuple(MODEL_SPECS), default="llama3b",
                     help="--component model: llama3b (config 3) or qwen7b (config 4)")
-    ap.add_argument("--component", choices=("attention", "prefill", "model"), default="attention",
+    ap.add_argument("--component", choices=("attention", "prefill", "model", "varlen"), default="attention",
                     help="prefill: time the Llama prefill companion kernels instead; model: Llama-3.2-3B prefill "
-                         "ms through the model API (tensor-parallel over the ranks under torchrun)")
+                         "ms through the model API (tensor-parallel over the ranks under torchrun); varlen: the "
+                         "long-context varlen sweep (config 5)")
     args = ap.parse_args()
     CFG["batch"] = args.batch
     if args.warmup < 3:
@@ -655,6 +767,8 @@ def main() -> None:
         run_prefill_components(args)
     elif args.component == "model":
         run_model_prefill(args)
+    elif args.component == "varlen":
+        run_varlen(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
