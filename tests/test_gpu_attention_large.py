@@ -70,3 +70,33 @@ def test_headline_config_with_outliers(cuda_device):
     assert diff.max() <= 3e-2, float(diff.max())
     over = int((diff > MAX_ABS).sum())
     assert over <= 5e-4 * diff.size, (over, diff.size)
+
+
+def test_long_sequence_chunked_item_order(cuda_device):
+    """One 25,600-token sequence with GQA group 3 gives each (sequence, KV head) unit 300
+    work-item levels, enough for the paired kernel to deal one unit's levels per round of the
+    grid (chunked order); sampled query blocks of all heads match the CPU oracle within the
+    north-star bound. The mask groups are 7 key tiles wide at this length."""
+    from tilemix_b200.attention.precision_maps import make_precision_bitmask
+    from tilemix_b200.attention.tilemix import device_error_code, tilemix_attention_with_quant
+    from tilemix_b200.models._attention_base import pick_mask_block_n
+
+    dev = cuda_device
+    T, hq, hk = 25600, 3, 1
+    bnm = pick_mask_block_n(T, 64)
+    q, k, v, cu = make_qkv([T], hq, hk, D, seed=11)
+    words = make_precision_bitmask(T, 128, bnm, None, 0.5, "sptrans", {"percentage": 0.5}, 64, device=dev)
+    out, _ = tilemix_attention_with_quant(q.to(dev), k.to(dev), v.to(dev), cu.to(dev), cu.to(dev), T, T, words,
+                                          block_m=128, block_n=64, block_n_mask=bnm, causal=True,
+                                          routing_mode="mixed", scalar_scales=True, int8_use_fp16_v=True)
+    torch.cuda.synchronize()
+    assert device_error_code(dev) == 0
+    blocks = [0, 1, 99, 198, 199]
+    ref = ora.tilemix_attention_with_quant(q.numpy(), k.numpy(), v.numpy(), cu.numpy(), cu.numpy(), T, T,
+                                           words.view(torch.int64).cpu().numpy().view(np.uint64), block_m=128,
+                                           block_n=64, block_n_mask=bnm, causal=True, routing_mode="mixed",
+                                           scalar_scales=True, int8_use_fp16_v=True, heads=list(range(hq)),
+                                           q_blocks=blocks)
+    rows = np.concatenate([np.arange(m * 128, (m + 1) * 128) for m in blocks])
+    diff = np.abs(out.float().cpu().numpy()[rows] - ref[rows].astype(np.float32))
+    assert diff.max() <= MAX_ABS and diff.mean() <= MEAN_ABS, (float(diff.max()), float(diff.mean()))

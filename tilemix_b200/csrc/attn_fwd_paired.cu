@@ -96,7 +96,11 @@ struct QTile {
 
 // One work item, resolved from its index. Items are ordered by level x (0 =
 // the first pair of each unit's tile list, the longest under causal masking),
-// then sequence, then KV head.
+// then sequence, then KV head, in chunks of g.chunk levels: (level chunk, unit,
+// level within the chunk). With chunk 1 that is level-major (all units' longest
+// items first). Units of many levels (long sequences) use a chunk of one grid's
+// worth, so the CTAs of a round work on one unit and stream its K/V through L2
+// together, while the chunks still run longest first.
 struct Item {
   QTile tl[2];
   int q_start, seqlen_q, k_start, seqlen_k;
@@ -107,15 +111,28 @@ struct Item {
 struct Grid {
   int nx, ny, nz, n_items;
   int mt;  // query blocks of the longest sequence
+  int chunk;  // levels per unit dealt together (1: level-major order)
 };
 
 __device__ __forceinline__ Item load_item(int it, const AttnArgs& a, const Grid& g) {
   Item m;
-  const int per_level = g.ny * g.nz;
-  const int x = it / per_level;
-  const int rem = it - x * per_level;
-  const int z = rem / g.ny;
-  const int y = rem - z * g.ny;
+  const int U = g.ny * g.nz;
+  const int C = g.chunk;
+  const int full = g.nx / C;
+  int x, unit;
+  if (it < full * C * U) {
+    const int k = it / (C * U);
+    const int r = it - k * C * U;
+    unit = r / C;
+    x = k * C + (r - unit * C);
+  } else {
+    const int Cl = g.nx - full * C;
+    const int r = it - full * C * U;
+    unit = r / Cl;
+    x = full * C + (r - unit * Cl);
+  }
+  const int z = unit / g.ny;
+  const int y = unit - z * g.ny;
   m.b = z;
   m.q_start = a.cu_q[z];
   m.seqlen_q = a.cu_q[z + 1] - m.q_start;
@@ -717,6 +734,8 @@ int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUten
   if (items > (1ll << 30)) return TM_ERR_SHAPE;
   g.n_items = static_cast<int>(items);
   const int ctas = static_cast<int>(std::min<int64_t>(items, n_sm[dev]));
+  // Long units (at least two grids' worth of levels): one unit's levels per round.
+  g.chunk = g.nx >= 2 * ctas ? ctas : 1;
   tilemix_attn_fwd_paired_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(q, k16, k8, v, a, g);
   return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
 }
