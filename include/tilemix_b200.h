@@ -154,11 +154,6 @@ typedef struct tm_attn_params {
   int causal, routing_mode, run_length, scalar_scales, int8_use_fp16_v;
   float sm_scale;
   int* error_flag; /* optional device int, set non-zero on a device-side timeout */
-  /* Optional device int[2], zero before the first call: work counter of the
-   * persistent kernel's dynamic scheduler (left at zero after every call).
-   * NULL = a counter inside the library, shared by all calls on a device, so
-   * calls that may overlap on the GPU must then each pass their own. */
-  int* sched_workspace;
 } tm_attn_params;
 
 /*
@@ -177,11 +172,9 @@ typedef struct tm_attn_tuning {
    * rounding of P for fewer rescales of the output accumulator. <= 15. */
   float rescale_threshold;
   /* Kernel selection: 0 = automatic (the paired kernel when head_dim is 128,
-   * block_m 128 and Q is quantised in kernel, else the general kernel);
-   * 1 = always the general kernel; 2 = the persistent route-compacted kernel
-   * where the paired one would apply; 3 = the paired kernel with 128-key
-   * softmax steps there; 4 = the paired kernel with each score row split
-   * across two softmax warps there. */
+   * block_m 128, Q is quantised in kernel, there is no bias and INT8 tiles use
+   * FP16 V; else the general kernel); 1 = always the general kernel. Other
+   * values return TM_ERR_SHAPE. */
   int force_general;
 } tm_attn_tuning;
 

@@ -46,7 +46,6 @@ class TmAttnParams(ctypes.Structure):
         ("int8_use_fp16_v", c_int),
         ("sm_scale", ctypes.c_float),
         ("error_flag", c_void_p),
-        ("sched_workspace", c_void_p),
     ]
 
 

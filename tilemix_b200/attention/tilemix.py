@@ -52,17 +52,6 @@ ROUTING_MODE_INT8 = 2
 RoutingMode = Literal["auto", "mixed", "fp16", "int8"]
 
 _ERROR_WORDS: dict[int, torch.Tensor] = {}
-_SCHED_WORDS: dict[int, torch.Tensor] = {}
-
-
-def _sched_word(device: torch.device) -> torch.Tensor:
-    """Per-device scheduler counters of the persistent kernel (left at zero by every launch)."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    w = _SCHED_WORDS.get(idx)
-    if w is None:
-        w = torch.zeros(2, dtype=torch.int32, device=torch.device("cuda", idx))
-        _SCHED_WORDS[idx] = w
-    return w
 
 
 def _error_word(device: torch.device) -> torch.Tensor:
@@ -134,35 +123,52 @@ def _routing_mode_code(mode: str) -> int:
 
 def classify_bitmask_routing(precision_bitmask: torch.Tensor, *, seqlen_q: int, seqlen_k: int, block_m: int,
                              block_n: int, block_n_mask: int, causal: bool) -> Literal["mixed", "fp16", "int8"]:
-    """Decide whether a map routes everything to one format (tilemix.py:968-1014)."""
+    """"fp16" / "int8" when every routing bit the kernel reads selects that format, else
+    "mixed" (the contract of tilemix.py:968-1014).
+
+    The bits a row reads are the mask groups its causal key range reaches; all rows are
+    tested at once with tensor ops on the map's own device, and only the two verdicts
+    cross to the host. The answer is remembered on the map tensor per argument set and
+    reused while the tensor is not modified in place (its version counter is unchanged),
+    so repeated ``routing_mode="auto"`` calls on a cached map cost no device sync.
+    """
     if block_n_mask % block_n != 0:
         raise ValueError("block_n_mask must be a multiple of block_n")
     m_blocks = (seqlen_q + block_m - 1) // block_m
-    compute_blocks = (seqlen_k + block_n - 1) // block_n
-    mask_group = block_n_mask // block_n
-    host_masks = precision_bitmask.detach().reshape(-1).cpu().tolist()
-    if len(host_masks) == 0 or len(host_masks) % m_blocks:
+    n_rows = precision_bitmask.numel()
+    if n_rows == 0 or m_blocks <= 0 or n_rows % m_blocks:
         raise ValueError("precision_bitmask has an invalid row count")
-    all_fp16 = True
-    all_int8 = True
-    for row, raw_mask in enumerate(host_masks):
-        query_block = row % m_blocks
-        row_blocks = compute_blocks
-        if causal:
-            numerator = (query_block + 1) * block_m + seqlen_k - seqlen_q
-            row_blocks = max(0, min(compute_blocks, (numerator + block_n - 1) // block_n))
-        route_blocks = (row_blocks + mask_group - 1) // mask_group
-        valid_mask = (1 << route_blocks) - 1 if route_blocks else 0
-        routed = (int(raw_mask) & ((1 << 64) - 1)) & valid_mask
-        all_fp16 &= routed == 0
-        all_int8 &= routed == valid_mask
-        if not all_fp16 and not all_int8:
-            return "mixed"
-    if all_fp16:
-        return "fp16"
-    if all_int8:
-        return "int8"
-    return "mixed"
+    key = (seqlen_q, seqlen_k, block_m, block_n, block_n_mask, bool(causal))
+    memo = getattr(precision_bitmask, "_tilemix_routing", None)
+    version = precision_bitmask._version
+    if memo is not None and memo.get(key, (None, None))[0] == version:
+        return memo[key][1]
+    words = precision_bitmask.detach().reshape(-1)
+    words = words.view(torch.int64) if words.dtype == torch.uint64 else words.to(torch.int64)
+    compute_blocks = (seqlen_k + block_n - 1) // block_n
+    group = block_n_mask // block_n
+    if causal:
+        query_block = torch.arange(n_rows, device=words.device, dtype=torch.int64) % m_blocks
+        first_hidden = (query_block + 1) * block_m + (seqlen_k - seqlen_q)
+        row_tiles = torch.div(first_hidden + block_n - 1, block_n, rounding_mode="floor").clamp(0, compute_blocks)
+    else:
+        row_tiles = torch.full((n_rows,), compute_blocks, device=words.device, dtype=torch.int64)
+    groups = torch.div(row_tiles + group - 1, group, rounding_mode="floor")
+    # Bits [0, groups) of each row; a row reaching past bit 63 can never be all-INT8.
+    all_ones = torch.full_like(groups, -1)
+    valid = torch.where(groups >= 64, all_ones, (torch.ones_like(groups) << groups.clamp(max=63)) - 1)
+    routed = words & valid
+    verdict = torch.stack([(routed == 0).all(), ((routed == valid) & (groups <= 64)).all()]).tolist()
+    mode = "fp16" if verdict[0] else ("int8" if verdict[1] else "mixed")
+    if memo is None:
+        memo = {}
+        try:
+            precision_bitmask._tilemix_routing = memo
+        except AttributeError:
+            memo = None
+    if memo is not None:
+        memo[key] = (version, mode)
+    return mode
 
 
 def _ptr(t: Optional[torch.Tensor]) -> ctypes.c_void_p:
@@ -209,11 +215,9 @@ def _launch(q, k, v, o, cu_q, cu_k, bitmask, max_q, max_k, *, q8=None, sq=None, 
     p.int8_use_fp16_v = int(bool(int8_use_fp16_v))
     p.sm_scale = float(sm_scale)
     p.error_flag = _ptr(_error_word(q.device))
-    p.sched_workspace = _ptr(_sched_word(q.device))
     tune = TmAttnTuning()
     tune.rescale_threshold = rescale_threshold() if threshold is None else float(threshold)
-    tune.force_general = {"general": 1, "persistent": 2, "paired128": 3, "split": 4}.get(
-        os.environ.get("TILEMIX_B200_KERNEL", "").strip().lower(), 0)
+    tune.force_general = 1 if os.environ.get("TILEMIX_B200_KERNEL", "").strip().lower() == "general" else 0
     stream = torch.cuda.current_stream(q.device).cuda_stream
     with torch.cuda.device(q.device):
         rc = lib().tm_attn_fwd_ex(ctypes.byref(p), ctypes.byref(tune), ctypes.c_void_p(stream))
@@ -319,15 +323,17 @@ def launch_prequantized(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q: int,
 
 
 def _quantize_k(k, cu_seqlens_k, max_seqlen_k, BLKK, equal_len: Optional[int] = None):
-    """K codes + fp16 block scales + int32 block offsets, without a host sync for equal lengths."""
+    """K codes + fp16 block scales + int32 block offsets, without a host sync: for varlen
+    batches the scale rows are allocated for the bound sum_b ceil(T_b / BLKK) <= tokens / BLKK
+    + batch, and the offsets stay on the device."""
     batch = cu_seqlens_k.numel() - 1
     if equal_len is not None:
         nblk = (equal_len + BLKK - 1) // BLKK
         cu_scale_i32 = torch.arange(0, (batch + 1) * nblk, nblk, device=k.device, dtype=torch.int32)
         n_rows = batch * nblk
     else:
-        cu_scale, cu_scale_i32 = _scale_offsets(cu_seqlens_k, BLKK, max_seqlen_k)
-        n_rows = int(cu_scale[-1].item())
+        _, cu_scale_i32 = _scale_offsets(cu_seqlens_k, BLKK, max_seqlen_k)
+        n_rows = k.shape[0] // BLKK + batch
     k8 = torch.empty(k.shape, dtype=torch.int8, device=k.device)
     sk16 = torch.empty((n_rows, k.shape[1]), dtype=torch.float16, device=k.device)
     cu_i32 = cu_seqlens_k.to(device=k.device, dtype=torch.int32).contiguous()

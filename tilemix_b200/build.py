@@ -20,9 +20,8 @@ INCLUDE = REPO_DIR / "include"
 LIB_NAME = "libtilemix_b200.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["attn_api.cu", "attn_fwd_general.cu", "attn_fwd_paired.cu", "attn_fwd_paired128.cu", "attn_fwd_split.cu",
-           "attn_fwd_persistent.cu", "quant.cu",
-           "precision_map.cu", "attn_noalloc.cu", "prefill.cu"]
+SOURCES = ["attn_api.cu", "attn_fwd_general.cu", "attn_fwd_paired.cu", "quant.cu", "precision_map.cu",
+           "attn_noalloc.cu", "prefill.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

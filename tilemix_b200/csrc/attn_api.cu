@@ -2,14 +2,8 @@
 // dispatch between the two sm_100a kernels:
 //   * paired  (attn_fwd_paired.cu): head_dim 128, block_m 128, Q quantised in
 //     kernel (or FP16-only routing) -- the model / tilemix_attention_with_quant path;
-//   * paired128 (attn_fwd_paired128.cu): the same shapes with 128-key softmax
-//     steps and one score slot per tile; selected explicitly (force_general == 3);
-//   * split (attn_fwd_split.cu): the same shapes with every score row shared by
-//     two softmax warps (16 softmax warps); selected explicitly (force_general == 4);
-//   * persistent (attn_fwd_persistent.cu): same shapes, route-compacted
-//     persistent schedule; selected explicitly (tuning.force_general == 2);
 //   * general (attn_fwd_general.cu): everything else the API accepts (block_m 64,
-//     head_dim 64, prequantised Q from launch_prequantized).
+//     head_dim 64, prequantised Q from launch_prequantized, bias, INT8-V).
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -24,12 +18,6 @@ int launch_attn_general(const CUtensorMap& k16, const CUtensorMap& k8, const CUt
                         int tiles, int heads_q, int batch, cudaStream_t stream);
 int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
                        const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
-int launch_attn_persistent(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
-                           const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
-int launch_attn_paired128(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
-                          const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
-int launch_attn_split(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
-                      const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -88,7 +76,7 @@ extern "C" int tm_attn_fwd(const tm_attn_params* p, void* stream) { return tm_at
 
 extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tuning, void* stream) {
   const float rescale_threshold = tuning ? tuning->rescale_threshold : 0.f;
-  const int kernel_choice = tuning ? tuning->force_general : 0;  // 0 auto, 1 general, 2 persistent, 3 paired128, 4 split
+  const int kernel_choice = tuning ? tuning->force_general : 0;  // 0 auto, 1 general
   const int force_general = kernel_choice == 1;
   using namespace tilemix;
   if (p == nullptr) return TM_ERR_NULL;
@@ -102,6 +90,7 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   if (p->block_n_mask <= 0 || p->block_n_mask % p->block_n != 0) return TM_ERR_SHAPE;
   if (p->routing_mode < 0 || p->routing_mode > 2) return TM_ERR_SHAPE;
   if (rescale_threshold < 0.f || rescale_threshold > 15.f) return TM_ERR_SHAPE;
+  if (kernel_choice != 0 && kernel_choice != 1) return TM_ERR_SHAPE;
   if (p->routing_mode == TM_ROUTE_MIXED && p->precision_bitmask == nullptr) return TM_ERR_NULL;
   const bool need_int8 = p->routing_mode != TM_ROUTE_FP16;
   const bool fuse_q = need_int8 && p->q8 == nullptr;
@@ -185,7 +174,6 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   a.qk_scale = p->sm_scale * 1.44269502162933349609375f;
   a.rescale_threshold = rescale_threshold;
   a.err = p->error_flag;
-  a.sched = p->sched_workspace;
   a.v8_path = v8_path ? 1 : 0;
   a.v_scale = static_cast<const __half*>(p->v_scale);
   a.cu_vs = p->cu_v_scale;
@@ -194,19 +182,11 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   a.b_sm = p->bias_stride[2];
   a.b_sn = p->bias_stride[3];
 
-  a.pair_heads = (a.group % 2 == 0) ? 1 : 0;
   if (p->heads_q > 65535 || p->batch > 65535) return TM_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // Bias and the INT8-V path run on the general kernel.
   const bool paired_ok = !force_general && D == 128 && p->block_m == 128 && (fuse_q || !need_int8) && !v8_path &&
                          p->bias == nullptr;
-  if (paired_ok && kernel_choice == 2) {
-    CUtensorMap m_q;
-    rc = make_map(&m_q, p->q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, p->heads_q, p->q_tokens, p->q_stride_head,
-                  p->q_stride_tok, 64, CU_TENSOR_MAP_SWIZZLE_128B, 128);
-    if (rc != TM_OK) return rc;
-    return launch_attn_persistent(m_q, m_k16, m_k8, m_v, a, p->batch, p->max_seqlen_q, st);
-  }
   if (paired_ok) {
     // The paired kernel fetches all 128 dims of a tile in one 4-D copy.
     CUtensorMap q4, k4, v4;
@@ -216,8 +196,6 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
     if (rc != TM_OK) return rc;
     rc = make_map_d128(&v4, p->v, p->heads_k, p->k_tokens, p->v_stride_head, p->v_stride_tok, 64);
     if (rc != TM_OK) return rc;
-    if (kernel_choice == 3) return launch_attn_paired128(q4, k4, m_k8, v4, a, p->batch, p->max_seqlen_q, st);
-    if (kernel_choice == 4) return launch_attn_split(q4, k4, m_k8, v4, a, p->batch, p->max_seqlen_q, st);
     return launch_attn_paired(q4, k4, m_k8, v4, a, p->batch, p->max_seqlen_q, st);
   }
   const int tiles = (p->max_seqlen_q + 127) / 128;

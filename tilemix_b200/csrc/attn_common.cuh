@@ -38,12 +38,10 @@ struct AttnArgs {
   int HQ, HK, group, D;
   int block_m, block_n_mask, blkq, blkk;
   int causal, mode, fuse_q;
-  int pair_heads;  // paired128 / split kernels: 1 = CTA holds two heads of one KV group, 0 = two m-tiles of one head
   int o_vec32;     // O rows start on 32-byte boundaries (out 32-byte aligned, strides multiples of 16)
   float qk_scale;
   float rescale_threshold;
   int* err;
-  int* sched;  // dynamic scheduler counters (int[2]) of the persistent kernel
   // INT8-V PV path (int8_use_fp16_v == 0, general kernel): fp16 V block scales.
   int v8_path;
   const __half* v_scale;

@@ -29,7 +29,6 @@ enum : int {
   kErrTimeoutPV = 5,        // waited too long for a PV completion
   kErrTimeoutQ = 6,         // MMA warp waited too long for Q in TMEM
   kErrTimeoutDrain = 7,     // final drain of in-flight work timed out
-  kErrTimeoutExchange = 8,  // partner thread of a split softmax row never published its value
   kErrTimeoutQFree = 9,     // Q producer waited too long for the previous work item's last S
   kErrTimeoutOFree = 10,    // MMA warp waited too long for the previous work item's O to be read
 };
