@@ -34,6 +34,19 @@ extern "C" {
 #define TM_ROUTE_FP16 1
 #define TM_ROUTE_INT8 2
 
+/* Numerics (no reference counterpart: they select which execution of the
+ * reference's arithmetic the results reproduce).
+ *   TM_NUMERICS_GPU    the reference's Triton kernels as they run on the GPU:
+ *                      FP16-route QK^T accumulated in fp16 by the tensor core
+ *                      (tl.dot(..., out_dtype=fp16)), fp32 divisions of the
+ *                      quantiser and of the final acc / l by the approximate
+ *                      PTX div.full.f32 that Triton emits for `/`. The default.
+ *   TM_NUMERICS_EXACT  the reference's algorithm in exact arithmetic, as its
+ *                      Triton interpreter runs it on the CPU: QK^T accumulated
+ *                      in fp32 and rounded once to fp16, IEEE divisions. */
+#define TM_NUMERICS_GPU 0
+#define TM_NUMERICS_EXACT 1
+
 /*
  * Per-block symmetric INT8 quantisation of a packed fp16 tensor.
  * Replaces quant_per_block_int8_kernel + per_block_int8_single
@@ -52,6 +65,15 @@ int tm_quant_per_block_int8(const void* x, int64_t x_stride_tok, int64_t x_strid
                             int dim, int blk, int max_seqlen, float sm_scale, int8_t* out,
                             int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32,
                             void* scale_f16, void* stream);
+
+/* tm_quant_per_block_int8 in the given TM_NUMERICS_* mode (tm_quant_per_block_int8
+ * is TM_NUMERICS_GPU): GPU numerics give the codes and scales of the reference's
+ * quantiser run on the GPU, exact numerics those of its interpreter run. */
+int tm_quant_per_block_int8_ex(const void* x, int64_t x_stride_tok, int64_t x_stride_head,
+                               const int32_t* cu_seqlens, const int32_t* cu_scale, int batch, int heads,
+                               int dim, int blk, int max_seqlen, float sm_scale, int8_t* out,
+                               int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32,
+                               void* scale_f16, int numerics, void* stream);
 
 /* Routing-map patterns of make_precision_bitmask (attention/precision_maps.py:404-636). */
 #define TM_MAP_ZERO 0
@@ -160,7 +182,7 @@ typedef struct tm_attn_params {
  * Fused FP16/INT8 tile-routed flash-attention forward (tcgen05 + TMA + TMEM).
  * Replaces attn_fwd (attention/triton/tilemix.py:503-951) as launched by
  * launch_prequantized (:1132-1336). Asynchronous on `stream`. Uses the
- * reference's softmax update rule (rescale_threshold 0).
+ * reference's softmax update rule (rescale_threshold 0) and TM_NUMERICS_GPU.
  */
 int tm_attn_fwd(const tm_attn_params* params, void* stream);
 
@@ -176,25 +198,36 @@ typedef struct tm_attn_tuning {
    * FP16 V; else the general kernel); 1 = always the general kernel. Other
    * values return TM_ERR_SHAPE. */
   int force_general;
+  /* TM_NUMERICS_GPU (0) or TM_NUMERICS_EXACT (1); also the numerics of the
+   * in-kernel Q quantisation. */
+  int numerics;
 } tm_attn_tuning;
 
-/* tm_attn_fwd with explicit tuning (NULL = defaults of tm_attn_fwd). */
+/* tm_attn_fwd with explicit tuning (NULL = defaults of tm_attn_fwd: threshold 0,
+ * automatic kernel, TM_NUMERICS_GPU). */
 int tm_attn_fwd_ex(const tm_attn_params* params, const tm_attn_tuning* tuning, void* stream);
 
 /*
  * tm_attn_fwd_ex for callers that cannot allocate device memory (no
  * counterpart in the reference): a host whose framework owns every device
  * allocation and hands the library only Q/K/V/O, or a plugin hook in which
- * allocating is not allowed, can still run the INT8 routes. The quantised K
- * operand that tm_attn_fwd takes from caller buffers is produced inside this
- * call into fixed-size scratch reserved by the library (16 MiB of K codes:
- * k_tokens * heads_k * head_dim <= 16,777,216; (k_tokens / blkk + batch) *
- * heads_k <= 262,144 scales; batch <= 65,535); larger problems return
- * TM_ERR_UNSUPPORTED. params->k8, k_scale and cu_k_scale must be NULL. The
- * call allocates nothing. The first call on a device resolves the scratch
- * address (a runtime query), so make it before capturing a stream. Calls that
- * may overlap on the GPU (several streams or threads) share the scratch and
- * must be serialised by the caller.
+ * allocating is not allowed. The quantised K operand that tm_attn_fwd takes
+ * from caller buffers is produced inside this call (in the numerics of
+ * `tuning`) into fixed-size scratch that the library's module holds on each
+ * device where it is loaded (loaded at the latest by the first call there):
+ * 16 MiB of K codes (k_tokens * heads_k * head_dim <= 16,777,216), 262,144 K
+ * scales ((k_tokens / blkk + batch) * heads_k <= 262,144) and batch <= 65,535;
+ * blkk must be 64 or 128. Larger problems return TM_ERR_UNSUPPORTED, and every
+ * argument is checked before anything is queued. params->k8, k_scale and
+ * cu_k_scale must be NULL. FP16-only routing needs no K operand and forwards
+ * to tm_attn_fwd_ex. The INT8-V PV path (int8_use_fp16_v == 0 with an INT8
+ * route) still reads v8 / v_scale / cu_v_scale from the caller: callers that
+ * pass only Q/K/V/O set int8_use_fp16_v = 1. The call allocates nothing. Its
+ * first call on a device resolves the scratch address (a runtime query, which
+ * can fail with TM_ERR_LAUNCH if the module cannot be loaded there), so make a
+ * warm-up call at initialisation, before any stream capture. Calls that may
+ * overlap on the GPU (several streams or threads) share the scratch and must
+ * be serialised by the caller.
  */
 int tm_attn_fwd_noalloc(const tm_attn_params* params, const tm_attn_tuning* tuning, void* stream);
 
@@ -212,13 +245,14 @@ int tm_attn_fwd_noalloc(const tm_attn_params* params, const tm_attn_tuning* tuni
  * attention (quant_per_block_varlen.py:6-45, sm_scale 1, blocks of blkk = 64 or
  * 128 tokens per sequence and KV head): k8 int8 [batch * seq_len, heads_k,
  * head_dim], optional k_scale_f16 / k_scale_f32 [batch * ceil(seq_len / blkk),
- * heads_k], bit-identical to tm_quant_per_block_int8 run on ok.
+ * heads_k], bit-identical to tm_quant_per_block_int8_ex run on ok with the
+ * same TM_NUMERICS_* mode `numerics`.
  */
 int tm_rotary_token_major(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, const void* k, int64_t k_sb,
                           int64_t k_sh, int64_t k_st, const void* cos, int64_t cos_sb, int64_t cos_st,
                           const void* sin, int64_t sin_sb, int64_t sin_st, int batch, int heads_q, int heads_k,
                           int seq_len, int head_dim, void* oq, void* ok, int8_t* k8, void* k_scale_f16,
-                          float* k_scale_f32, int blkk, void* stream);
+                          float* k_scale_f32, int blkk, int numerics, void* stream);
 
 /* out = fp16(fp16(silu(gate)) * up) elementwise over n fp16 values; replaces
  * silu_mul / _silu_mul (:825-866). */

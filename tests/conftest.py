@@ -20,3 +20,12 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda", 0)
+
+
+@pytest.fixture
+def exact_numerics(monkeypatch):
+    """Run the library in exact numerics (IEEE divisions, fp32-accumulated scores): the
+    arithmetic of the CPU oracle and of the reference's interpreter fixtures, so comparisons
+    against them are tight. The default numerics reproduce the reference's GPU run instead
+    (tests/test_gpu_reference_triton.py)."""
+    monkeypatch.setenv("TILEMIX_B200_NUMERICS", "exact")

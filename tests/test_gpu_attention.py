@@ -11,7 +11,8 @@ import torch
 from oracle import attention_oracle as ora
 from tests.helpers import err_stats, make_bias, make_qkv, random_bitmask
 
-pytestmark = pytest.mark.gpu
+# Compared with the CPU oracle / interpreter fixtures: exact numerics.
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("exact_numerics")]
 
 MAX_ABS = 2e-3
 MEAN_ABS = 2e-4
@@ -68,9 +69,15 @@ def test_attention_matches_oracle(cuda_device, lens, hq, hk, d, block_m, bnm, mo
 
 
 def test_attention_outlier_channels(cuda_device):
-    """Config-2 style inputs: 4 fixed outlier channels per head scaled x20."""
-    mx, mean = _run_case([1024], 3, 1, 128, 128, mode="mixed", outliers=4, threshold=0.0)
-    assert mean <= MEAN_ABS, (mx, mean)
+    """Config-2 style inputs: 4 fixed outlier channels per head scaled x20. Rows dominated by
+    a key whose score lies at an fp16 rounding midpoint can move by ~1e-2 against the oracle
+    (test_gpu_attention_large.py explains the two rounding cases; the reference's own GPU run
+    departs from the oracle further), so the bound is the mean, the share of elements over
+    2e-3 and the largest error."""
+    diff = _run_case([1024], 3, 1, 128, 128, mode="mixed", outliers=4, threshold=0.0, return_diff=True)
+    assert diff.mean() <= MEAN_ABS, float(diff.mean())
+    assert diff.max() <= 3e-2, float(diff.max())
+    assert int((diff > MAX_ABS).sum()) <= 5e-4 * diff.size
 
 
 def test_attention_non_causal(cuda_device):

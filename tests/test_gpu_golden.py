@@ -11,7 +11,8 @@ import torch
 
 from tests.helpers import make_bias, make_qkv
 
-pytestmark = pytest.mark.gpu
+# Compared with the CPU oracle / interpreter fixtures: exact numerics.
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("exact_numerics")]
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 MAX_ABS = 2e-3

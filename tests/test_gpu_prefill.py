@@ -12,7 +12,8 @@ import torch
 
 from oracle import prefill_oracle as po
 
-pytestmark = pytest.mark.gpu
+# Compared with the CPU oracle / interpreter fixtures: exact numerics.
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("exact_numerics")]
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 

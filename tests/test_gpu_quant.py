@@ -6,7 +6,8 @@ import torch
 from oracle import attention_oracle as ora
 from tests.helpers import make_qkv
 
-pytestmark = pytest.mark.gpu
+# Compared with the CPU oracle / interpreter fixtures: exact numerics.
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("exact_numerics")]
 
 
 @pytest.mark.parametrize("lens,h,d,blk", [([512], 4, 64, 128), ([4096, 1000, 1], 8, 128, 64),

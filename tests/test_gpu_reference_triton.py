@@ -1,0 +1,145 @@
+"""Parity with the reference's own Triton kernels run on the same GPU.
+
+The reference (attention/triton/tilemix.py and quant_per_block_varlen.py,
+unmodified, installed under baseline/_ref) is imported by this test process
+only; the package never imports it. Each case runs the reference's
+``tilemix_attention_with_quant`` (Q/K quantisation + attn_fwd, one autotune
+configuration forced as its prefill benchmark does) and this package's drop-in
+of the same function on identical device inputs, in the package's default
+numerics, which reproduce the reference's GPU arithmetic (FP16-route QK^T
+accumulated in fp16 by the tensor core, the approximate ``div.full.f32`` for
+the quantiser's and the output's divisions).
+
+Bounds: the north-star bound, max-abs 2e-3 and mean-abs 2e-4 on the fp16
+outputs, over every element; the quantiser's codes and scales bit for bit.
+Cases: config 1 (1 x 512, 4/4 heads, head_dim 64, sptrans), config 2 (8 x 4096,
+24/8 heads, head_dim 128) with the benchmark's outlier channels for sptrans /
+zero / one, the INT8-V PV path (the API's default ``int8_use_fp16_v=False``),
+a ragged varlen GQA batch and an additive bias.
+"""
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+from tests.helpers import make_bias, make_qkv
+
+pytestmark = pytest.mark.gpu
+
+REF_ROOT = Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+MAX_ABS = 2e-3
+MEAN_ABS = 2e-4
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not (REF_ROOT / "attention" / "triton" / "tilemix.py").exists():
+        pytest.skip("the reference is not installed under baseline/_ref")
+    if str(REF_ROOT) not in sys.path:
+        sys.path.append(str(REF_ROOT))
+    import attention.triton.quant_per_block_varlen as ref_quant
+    import attention.triton.tilemix as ref_tmx
+
+    return ref_tmx, ref_quant
+
+
+@pytest.fixture
+def gpu_numerics(monkeypatch):
+    monkeypatch.setenv("TILEMIX_B200_NUMERICS", "gpu")
+    monkeypatch.setenv("TILEMIX_B200_RESCALE_THRESHOLD", "0")
+
+
+def _map(dev, T, block_m, block_n_mask, pattern, hk):
+    from tilemix_b200.attention.precision_maps import make_precision_bitmask
+
+    params = {"percentage": 0.5} if pattern not in ("zero", "one") else {}
+    words = make_precision_bitmask(T, block_m, block_n_mask, None, 0.5, pattern, params, 64, device=dev)
+    return words.view(torch.int64).repeat(hk).view(torch.uint64)
+
+
+def _compare(ref, monkeypatch, dev, lens, hq, hk, d, block_m, pattern, mode, outliers=0, fp16_v=True, bias_seed=None,
+             seed=0):
+    from tilemix_b200.attention.tilemix import device_error_code, tilemix_attention_with_quant
+
+    ref_tmx, _ = ref
+    T = max(lens)
+    bnm = 64
+    q, k, v, cu = make_qkv(lens, hq, hk, d, seed=seed, outliers=outliers)
+    q, k, v, cu = q.to(dev), k.to(dev), v.to(dev), cu.to(dev)
+    pm = _map(dev, T, block_m, bnm, pattern, hk)
+    bias = None if bias_seed is None else make_bias(len(lens), hq, T, bias_seed).to(dev)
+    kw = dict(block_m=block_m, block_n=64, block_n_mask=bnm, causal=True, routing_mode=mode,
+              scalar_scales=block_m == 128, int8_use_fp16_v=fp16_v, bias=bias)
+    monkeypatch.setenv("TILEMIX_FORCE_CONFIG", "128,64,8,2,0" if block_m == 128 else "64,64,4,2,0")
+    o_ref, mode_ref = ref_tmx.tilemix_attention_with_quant(q, k, v, cu, cu, T, T, pm, **kw)
+    o, mode_ours = tilemix_attention_with_quant(q, k, v, cu, cu, T, T, pm, **kw)
+    torch.cuda.synchronize()
+    assert device_error_code(dev) == 0
+    assert mode_ours == mode_ref
+    diff = (o.float() - o_ref.float()).abs()
+    return float(diff.max()), float(diff.mean())
+
+
+def test_quantiser_bit_identical_to_reference_gpu(cuda_device, ref, gpu_numerics):
+    """Codes and fp32 scales of the reference's Triton quantiser on the GPU, bit for bit:
+    config-2 Q (blocks of 128) and K (blocks of 64) with outlier channels, and a ragged
+    batch with a zero block."""
+    from tilemix_b200.attention.quant_per_block_varlen import per_block_int8_single
+
+    _, ref_quant = ref
+    dev = cuda_device
+    q, k, _, cu = make_qkv([4096] * 8, 24, 8, 128, seed=0, outliers=4)
+    q2, _, _, cu2 = make_qkv([300, 1000, 129], 5, 1, 64, seed=7, outliers=2)
+    q2[300:428, 2] = 0.0  # an all-zero block
+    for x, c, T, blk in ((q, cu, 4096, 128), (k, cu, 4096, 64), (q2, cu2, 1000, 64), (q2, cu2, 1000, 128)):
+        x, c = x.to(dev), c.to(dev)
+        a8, asc, acu = ref_quant.per_block_int8_single(x, c, T, BLK=blk, sm_scale=1.0)
+        b8, bsc, bcu = per_block_int8_single(x, c, T, BLK=blk, sm_scale=1.0)
+        torch.cuda.synchronize()
+        assert torch.equal(acu.to(torch.int64), bcu.to(torch.int64))
+        assert torch.equal(asc.view(torch.int32), bsc.view(torch.int32))
+        assert torch.equal(a8, b8)
+
+
+@pytest.mark.parametrize("pattern,mode", [("sptrans", "mixed"), ("zero", "auto"), ("one", "auto")])
+def test_config1_matches_reference_gpu(cuda_device, ref, gpu_numerics, monkeypatch, pattern, mode):
+    mx, mean = _compare(ref, monkeypatch, cuda_device, [512], 4, 4, 64, 64, pattern, mode)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.parametrize("pattern,mode", [("sptrans", "mixed"), ("zero", "fp16"), ("one", "int8")])
+def test_config2_outliers_match_reference_gpu(cuda_device, ref, gpu_numerics, monkeypatch, pattern, mode):
+    """The benchmark's workload: 8 x 4096 tokens, 24 / 8 heads, 4 outlier channels x20."""
+    mx, mean = _compare(ref, monkeypatch, cuda_device, [4096] * 8, 24, 8, 128, 128, pattern, mode, outliers=4)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+def test_config2_int8_v_path_matches_reference_gpu(cuda_device, ref, gpu_numerics, monkeypatch):
+    """The API's default int8_use_fp16_v=False: INT8-routed tiles take the INT8-V PV path."""
+    mx, mean = _compare(ref, monkeypatch, cuda_device, [4096] * 8, 24, 8, 128, 128, "sptrans", "mixed", outliers=4,
+                        fp16_v=False)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.parametrize("block_m,d", [(128, 128), (64, 64)])
+def test_ragged_gqa_batch_matches_reference_gpu(cuda_device, ref, gpu_numerics, monkeypatch, block_m, d):
+    mx, mean = _compare(ref, monkeypatch, cuda_device, [1000, 257, 2048, 64], 6, 2, d, block_m, "bigbird", "mixed",
+                        outliers=2, seed=5)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+def test_bias_matches_reference_gpu(cuda_device, ref, gpu_numerics, monkeypatch):
+    mx, mean = _compare(ref, monkeypatch, cuda_device, [512, 384], 4, 2, 128, 128, "sptrans", "mixed", seed=9,
+                        bias_seed=21)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+def test_exact_numerics_within_bound_of_reference_gpu(cuda_device, ref, monkeypatch):
+    """The switch: on N(0, 1) inputs the exact numerics stay within the north-star bound of
+    the reference's GPU run as well (they differ from it only in the fp16 accumulation of
+    FP16-route scores and the approximate divisions)."""
+    monkeypatch.setenv("TILEMIX_B200_NUMERICS", "exact")
+    monkeypatch.setenv("TILEMIX_B200_RESCALE_THRESHOLD", "0")
+    mx, mean = _compare(ref, monkeypatch, cuda_device, [512], 4, 4, 64, 64, "sptrans", "mixed")
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)

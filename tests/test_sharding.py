@@ -13,7 +13,8 @@ import torch.multiprocessing as mp
 
 from oracle import attention_oracle as ora
 from tests.helpers import make_qkv, random_bitmask
-from tilemix_b200.sharding import pack_units, plan_units, sharded_attention, unit_cost, unpack_units
+from tilemix_b200.sharding import (head_block_views, kv_head_block, pack_units, plan_units, sharded_attention,
+                                   unit_cost, unpack_units)
 
 LENS, HQ, HK, D, BM = [130, 64, 200, 17], 4, 2, 64, 64
 
@@ -81,3 +82,32 @@ def test_two_rank_gloo_matches_unsharded(tmp_path):
                                             block_n=64, block_n_mask=64, causal=True, routing_mode="mixed",
                                             scalar_scales=False, int8_use_fp16_v=True)
     assert np.array_equal(got.numpy().view(np.uint16), full.view(np.uint16))
+
+
+def test_kv_head_blocks_partition_the_heads():
+    for heads_k in (1, 2, 4, 8):
+        for world in (1, 2, 4, 8):
+            blocks = [kv_head_block(heads_k, world, r) for r in range(world)]
+            if heads_k % world:
+                assert all(b is None for b in blocks)
+                continue
+            assert blocks[0][0] == 0 and blocks[-1][1] == heads_k
+            assert all(b[1] == n[0] for b, n in zip(blocks, blocks[1:]))
+            assert len({b[1] - b[0] for b in blocks}) == 1
+
+
+def test_head_block_views_assemble_the_unsharded_output():
+    """Equal-length batch (the bench's and the model's): each KV-head block run on its views
+    (the oracle standing in for the kernel) writes its slice of the full output in place;
+    the union over the blocks equals the unsharded call bit for bit, with a map whose rows
+    differ per KV head."""
+    lens = [150, 150, 150]
+    q, k, v, cu = make_qkv(lens, HQ, HK, D, seed=4, outliers=1)
+    mb = (150 + BM - 1) // BM
+    pm = random_bitmask(HK * mb, seed=2)
+    full = _oracle_attn(q, k, v, cu, 150, pm)
+    out = torch.zeros_like(q)
+    for r in range(2):
+        qv, kv, vv, ov, pmv = head_block_views(q, k, v, out, pm, mb, kv_head_block(HK, 2, r))
+        ov.copy_(_oracle_attn(qv.contiguous(), kv.contiguous(), vv.contiguous(), cu, 150, pmv.contiguous()))
+    assert torch.equal(out, full)

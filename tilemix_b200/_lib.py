@@ -14,6 +14,28 @@ LIB_PATH = Path(os.environ.get("TILEMIX_B200_LIB", _PKG / "libtilemix_b200.so"))
 
 TM_OK = 0
 TM_ROUTE_MIXED, TM_ROUTE_FP16, TM_ROUTE_INT8 = 0, 1, 2
+TM_NUMERICS_GPU, TM_NUMERICS_EXACT = 0, 1
+
+
+def numerics_mode() -> str:
+    """The numerics every op of the package computes in (``TILEMIX_B200_NUMERICS``):
+
+    ``"gpu"`` (default): the reference's Triton kernels as they execute on the GPU (FP16-route
+    QK^T accumulated in fp16 by the tensor core, the quantiser's and the output's fp32
+    divisions by the approximate ``div.full.f32`` that Triton emits for ``/``); outputs then
+    match the reference run on the same GPU. ``"exact"``: the same algorithm in exact
+    arithmetic (fp32 accumulation rounded once, IEEE divisions), as the reference's Triton
+    interpreter runs it on the CPU.
+    """
+    mode = os.environ.get("TILEMIX_B200_NUMERICS", "gpu").strip().lower()
+    if mode not in ("gpu", "exact"):
+        raise ValueError(f"TILEMIX_B200_NUMERICS must be 'gpu' or 'exact', got {mode!r}")
+    return mode
+
+
+def numerics_code() -> int:
+    """TM_NUMERICS_* value of :func:`numerics_mode`."""
+    return TM_NUMERICS_GPU if numerics_mode() == "gpu" else TM_NUMERICS_EXACT
 
 c_i64 = ctypes.c_int64
 c_int = ctypes.c_int
@@ -52,7 +74,7 @@ class TmAttnParams(ctypes.Structure):
 class TmAttnTuning(ctypes.Structure):
     """Mirror of ``tm_attn_tuning`` (include/tilemix_b200.h)."""
 
-    _fields_ = [("rescale_threshold", ctypes.c_float), ("force_general", c_int)]
+    _fields_ = [("rescale_threshold", ctypes.c_float), ("force_general", c_int), ("numerics", c_int)]
 
 
 class TmMapParams(ctypes.Structure):
@@ -71,6 +93,9 @@ SIGNATURES = {
     "tm_quant_per_block_int8": (c_int, [c_void_p, c_i64, c_i64, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                         c_int, ctypes.c_float, c_void_p, c_i64, c_i64, c_void_p, c_void_p,
                                         c_void_p]),
+    "tm_quant_per_block_int8_ex": (c_int, [c_void_p, c_i64, c_i64, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                           c_int, ctypes.c_float, c_void_p, c_i64, c_i64, c_void_p, c_void_p,
+                                           c_int, c_void_p]),
     "tm_attn_fwd": (c_int, [ctypes.POINTER(TmAttnParams), c_void_p]),
     "tm_attn_fwd_ex": (c_int, [ctypes.POINTER(TmAttnParams), ctypes.POINTER(TmAttnTuning), c_void_p]),
     "tm_attn_fwd_noalloc": (c_int, [ctypes.POINTER(TmAttnParams), ctypes.POINTER(TmAttnTuning), c_void_p]),
@@ -78,7 +103,7 @@ SIGNATURES = {
     "tm_rotary_token_major": (c_int, [c_void_p, c_i64, c_i64, c_i64, c_void_p, c_i64, c_i64, c_i64,
                                       c_void_p, c_i64, c_i64, c_void_p, c_i64, c_i64, c_int, c_int, c_int,
                                       c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
-                                      c_void_p]),
+                                      c_int, c_void_p]),
     "tm_silu_mul": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_void_p]),
     "tm_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, ctypes.c_float, c_void_p]),
     "tm_status_string": (ctypes.c_char_p, [c_int]),

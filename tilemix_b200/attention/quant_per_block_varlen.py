@@ -3,7 +3,9 @@
 
 Same functions, arguments and return values as the reference
 (quant_per_block_varlen.py:48-106); the work runs in the sm_100a kernel
-``tm_quant_per_block_int8`` of ``libtilemix_b200.so``.
+``tm_quant_per_block_int8_ex`` of ``libtilemix_b200.so``, in the numerics of
+``tilemix_b200._lib.numerics_mode`` (by default the reference's GPU arithmetic, so
+codes and scales equal those of its Triton quantiser run on the GPU).
 """
 from __future__ import annotations
 
@@ -12,7 +14,7 @@ from typing import Optional
 
 import torch
 
-from tilemix_b200._lib import check, lib
+from tilemix_b200._lib import check, lib, numerics_code
 
 
 def _scale_offsets(cu_seqlens: torch.Tensor, BLK: int, max_seqlen: int):
@@ -33,15 +35,15 @@ def _launch_quant(x: torch.Tensor, cu_seqlens_i32: torch.Tensor, cu_scale_i32: t
     batch = cu_seqlens_i32.numel() - 1
     stream = torch.cuda.current_stream(x.device).cuda_stream
     with torch.cuda.device(x.device):
-        rc = lib().tm_quant_per_block_int8(
+        rc = lib().tm_quant_per_block_int8_ex(
             ctypes.c_void_p(x.data_ptr()), x.stride(0), x.stride(1),
             ctypes.c_void_p(cu_seqlens_i32.data_ptr()), ctypes.c_void_p(cu_scale_i32.data_ptr()),
             batch, x.shape[1], x.shape[2], BLK, int(max_seqlen), float(sm_scale),
             ctypes.c_void_p(out.data_ptr()), out.stride(0), out.stride(1),
             ctypes.c_void_p(scale_f32.data_ptr() if scale_f32 is not None else 0),
             ctypes.c_void_p(scale_f16.data_ptr() if scale_f16 is not None else 0),
-            ctypes.c_void_p(stream))
-    check(rc, "tm_quant_per_block_int8")
+            numerics_code(), ctypes.c_void_p(stream))
+    check(rc, "tm_quant_per_block_int8_ex")
 
 
 def per_block_int8_single(x, cu_seqlens_x, max_seqlen_x, BLK=128, sm_scale=1.0):

@@ -23,12 +23,15 @@ results:
   * the online softmax is updated per 64-key tile for any ``block_n`` that is a
     multiple of 64 (the reference updates once per ``block_n`` tile); keys the
     reference visits beyond the causal limit are fully masked either way.
-Environment: ``TILEMIX_B200_RESCALE_THRESHOLD`` (log2 units, default 15): the
-running softmax max is moved only when a tile max exceeds it by more than this
-amount; 0 reproduces the reference's update-on-every-increase exactly. P then
-stays below 2^15, inside fp16's range; a running max that lags the true one
-scales every weight by the same power of two, which leaves P's relative fp16
-rounding unchanged and only moves small weights away from underflow.
+Environment:
+  * ``TILEMIX_B200_NUMERICS`` = ``gpu`` (default) / ``exact``: which execution of
+    the reference's arithmetic the results reproduce, its kernels on the GPU or
+    its algorithm in exact arithmetic (``tilemix_b200._lib.numerics_mode``);
+  * ``TILEMIX_B200_RESCALE_THRESHOLD`` (log2 units, default 0, at most 15): 0 is
+    the reference's softmax rule (the running max moves on every increase); with
+    t > 0 it moves only when a tile max exceeds it by more than t, so P stays
+    below 2^t and the output accumulator is rescaled less often, at the cost of
+    P's fp16 rounding differing from the reference's where the max lags.
 """
 from __future__ import annotations
 
@@ -38,7 +41,7 @@ from typing import Literal, Optional
 
 import torch
 
-from tilemix_b200._lib import TmAttnParams, TmAttnTuning, check, lib
+from tilemix_b200._lib import TmAttnParams, TmAttnTuning, check, lib, numerics_code, numerics_mode  # noqa: F401
 from tilemix_b200.attention.quant_per_block_varlen import (
     _launch_quant,
     _scale_offsets,
@@ -78,7 +81,8 @@ def device_error_code(device: Optional[torch.device] = None, reset: bool = True)
 
 
 def rescale_threshold() -> float:
-    return float(os.environ.get("TILEMIX_B200_RESCALE_THRESHOLD", "15"))
+    """Softmax rescale threshold (``TILEMIX_B200_RESCALE_THRESHOLD``, default 0: the reference's rule)."""
+    return float(os.environ.get("TILEMIX_B200_RESCALE_THRESHOLD", "0"))
 
 
 def _scale_dtype(dtype: torch.dtype) -> torch.dtype:
@@ -218,6 +222,7 @@ def _launch(q, k, v, o, cu_q, cu_k, bitmask, max_q, max_k, *, q8=None, sq=None, 
     tune = TmAttnTuning()
     tune.rescale_threshold = rescale_threshold() if threshold is None else float(threshold)
     tune.force_general = 1 if os.environ.get("TILEMIX_B200_KERNEL", "").strip().lower() == "general" else 0
+    tune.numerics = numerics_code()
     stream = torch.cuda.current_stream(q.device).cuda_stream
     with torch.cuda.device(q.device):
         rc = lib().tm_attn_fwd_ex(ctypes.byref(p), ctypes.byref(tune), ctypes.c_void_p(stream))

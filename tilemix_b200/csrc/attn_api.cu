@@ -72,13 +72,14 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 }  // namespace tilemix
 
-extern "C" int tm_attn_fwd(const tm_attn_params* p, void* stream) { return tm_attn_fwd_ex(p, nullptr, stream); }
+namespace tilemix {
 
-extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tuning, void* stream) {
+// Host-side argument checks of tm_attn_fwd_ex; no CUDA call. TM_OK when the
+// call would be launched (or is an empty problem), else the status it returns.
+int check_attn_args(const tm_attn_params* p, const tm_attn_tuning* tuning) {
   const float rescale_threshold = tuning ? tuning->rescale_threshold : 0.f;
   const int kernel_choice = tuning ? tuning->force_general : 0;  // 0 auto, 1 general
-  const int force_general = kernel_choice == 1;
-  using namespace tilemix;
+  const int numerics = tuning ? tuning->numerics : TM_NUMERICS_GPU;
   if (p == nullptr) return TM_ERR_NULL;
   if (p->q == nullptr || p->k == nullptr || p->v == nullptr || p->out == nullptr || p->cu_seqlens_q == nullptr ||
       p->cu_seqlens_k == nullptr)
@@ -91,6 +92,7 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   if (p->routing_mode < 0 || p->routing_mode > 2) return TM_ERR_SHAPE;
   if (rescale_threshold < 0.f || rescale_threshold > 15.f) return TM_ERR_SHAPE;
   if (kernel_choice != 0 && kernel_choice != 1) return TM_ERR_SHAPE;
+  if (numerics != TM_NUMERICS_GPU && numerics != TM_NUMERICS_EXACT) return TM_ERR_SHAPE;
   if (p->routing_mode == TM_ROUTE_MIXED && p->precision_bitmask == nullptr) return TM_ERR_NULL;
   const bool need_int8 = p->routing_mode != TM_ROUTE_FP16;
   const bool fuse_q = need_int8 && p->q8 == nullptr;
@@ -119,6 +121,25 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   }
   if (v8_path && (!aligned16(p->v8) || p->v8_stride_tok % 16 != 0 || p->v8_stride_head % 16 != 0))
     return TM_ERR_ALIGN;
+  if (p->heads_q > 65535 || p->batch > 65535) return TM_ERR_SHAPE;
+  return TM_OK;
+}
+
+}  // namespace tilemix
+
+extern "C" int tm_attn_fwd(const tm_attn_params* p, void* stream) { return tm_attn_fwd_ex(p, nullptr, stream); }
+
+extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tuning, void* stream) {
+  using namespace tilemix;
+  const int rc0 = check_attn_args(p, tuning);
+  if (rc0 != TM_OK) return rc0;
+  if (p->batch == 0 || p->max_seqlen_q == 0) return TM_OK;
+  const float rescale_threshold = tuning ? tuning->rescale_threshold : 0.f;
+  const int force_general = tuning ? tuning->force_general == 1 : 0;
+  const int numerics = tuning ? tuning->numerics : TM_NUMERICS_GPU;
+  const bool need_int8 = p->routing_mode != TM_ROUTE_FP16;
+  const bool fuse_q = need_int8 && p->q8 == nullptr;
+  const bool v8_path = need_int8 && !p->int8_use_fp16_v;
   const int D = p->head_dim;
   CUtensorMap m_k16, m_k8, m_v;
   int rc = make_map(&m_k16, p->k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, p->heads_k, p->k_tokens, p->k_stride_head,
@@ -173,6 +194,7 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   // qk_scale = fp32(sm_scale) * fp32(log2 e), as the reference evaluates it (:639).
   a.qk_scale = p->sm_scale * 1.44269502162933349609375f;
   a.rescale_threshold = rescale_threshold;
+  a.numerics = numerics == TM_NUMERICS_GPU ? kNumericsGpu : kNumericsExact;
   a.err = p->error_flag;
   a.v8_path = v8_path ? 1 : 0;
   a.v_scale = static_cast<const __half*>(p->v_scale);
@@ -182,7 +204,6 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   a.b_sm = p->bias_stride[2];
   a.b_sn = p->bias_stride[3];
 
-  if (p->heads_q > 65535 || p->batch > 65535) return TM_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // Bias and the INT8-V path run on the general kernel.
   const bool paired_ok = !force_general && D == 128 && p->block_m == 128 && (fuse_q || !need_int8) && !v8_path &&

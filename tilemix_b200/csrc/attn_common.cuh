@@ -3,16 +3,19 @@
 // The per-tile softmax below is the reference's _softmax_prefix_update
 // (attention/triton/tilemix.py:179-207) applied to one 64-key score tile held
 // in tensor memory, for the one query row owned by the calling thread:
-//   qk   = fp16(S)                                (FP16 route, fp32 accumulated S)
+//   qk   = fp16(S)                                (FP16 route, :254)
 //        = fp16(f32(S_i32) * score_scale)         (INT8 route, :401-404)
 //   keys at or beyond `lim` are masked to -inf    (causal / length, :256-262)
 //   p    = fp16(exp2(f32(qk) - m))                (:195-199)
-//   l   += sum exp2(f32(qk) - m)                 (:200, :206; summed before the
-//          fp16 rounding of p, a difference below fp16 resolution)
+//   l    = l * alpha + sum f32(p)                 (:200, :206)
 // where m is the row's reference maximum. With threshold 0 it is updated on
 // every increase (the reference's rule); with threshold t > 0 it only moves
 // when the tile max exceeds it by more than t (log2 units), which bounds
 // p by 2^t and makes rescaling of the output accumulator rare.
+// FP16-route scores arrive in TMEM as the MMA accumulated them: fp16 (one
+// value in the low half of each 32-bit column) in GPU numerics, where the
+// reference's tl.dot(..., out_dtype=fp16) accumulates in fp16 on the tensor
+// core, or fp32 rounded once in exact numerics (common.cuh).
 #pragma once
 
 #include "common.cuh"
@@ -39,6 +42,7 @@ struct AttnArgs {
   int block_m, block_n_mask, blkq, blkk;
   int causal, mode, fuse_q;
   int o_vec32;     // O rows start on 32-byte boundaries (out 32-byte aligned, strides multiples of 16)
+  int numerics;    // kNumericsGpu or kNumericsExact (common.cuh)
   float qk_scale;
   float rescale_threshold;
   int* err;
@@ -57,11 +61,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
   tmem_st16(taddr + 16, r + 16);
 }
 
-// Exact int32 -> fp32 for |x| < 2^22 without the conversion pipe: the bit
-// pattern of 1.5*2^23 plus x is the float 1.5*2^23 + x; subtracting 1.5*2^23
-// is exact. INT8 scores are bounded by 128 * 127 * 127 < 2^21.
-__device__ __forceinline__ float i2f_exact(uint32_t x) { return __uint_as_float(x + 0x4B400000u) - 12582912.0f; }
-
 __device__ __forceinline__ uint64_t f32x2_pack(float lo, float hi) {
   return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
 }
@@ -74,24 +73,9 @@ __device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
   return r;
 }
 
-__device__ __forceinline__ uint64_t f32x2_sub(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f32x2_add_rm(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
 __device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
 }
 // f32(lo or hi half of an fp16 pair) + c, one rounding, on the FMA pipe.
@@ -111,47 +95,21 @@ __device__ __forceinline__ uint32_t hmax2_u32(uint32_t a, uint32_t b) {
   return r;
 }
 
-// 2^x for a pair of x in [-126, 16) without the MUFU pipe: x = j + f with
-// j = floor(x) (an add rounded toward -inf against 1.5 * 2^23 leaves j in the
-// low mantissa bits), 2^f on [0, 1) by a degree-5 polynomial in Horner form
-// (relative-error minimax fit by the Remez exchange: max relative error
-// 1.5e-7 evaluated in fp32, the accuracy class of ex2.approx), and 2^j added to
-// the exponent field as an integer. Spreads part of the softmax exponentials
-// over the FMA pipe: the MUFU pipe (16 results per clock per SM) is the
-// softmax's throughput limit otherwise.
-__device__ __forceinline__ void exp2_poly_x2(float x0, float x1, float& e0, float& e1) {
-  const uint64_t kMagic = 0x4B4000004B400000ull;  // (1.5 * 2^23, 1.5 * 2^23)
-  const uint64_t x = f32x2_pack(x0, x1);
-  const uint64_t t = f32x2_add_rm(x, kMagic);    // 1.5 * 2^23 + floor(x), exact
-  const uint64_t f = f32x2_add(x, f32x2_sub(kMagic, t));  // x - floor(x) in [0, 1), exact
-  uint64_t p = f32x2_fma(0x3AF619053AF61905ull, f, 0x3C1348063C134806ull);
-  p = f32x2_fma(p, f, 0x3D64AA233D64AA23ull);
-  p = f32x2_fma(p, f, 0x3E75EAD43E75EAD4ull);
-  p = f32x2_fma(p, f, 0x3F31727B3F31727Bull);
-  p = f32x2_fma(p, f, 0x3F7FFFFF3F7FFFFFull);
-  // (1.5 * 2^23 + j) << 23 == j << 23 modulo 2^32.
-  e0 = __uint_as_float(static_cast<uint32_t>(p) + (static_cast<uint32_t>(t) << 23));
-  e1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(t >> 32) << 23));
-}
-
-// Pairs of a 64-key tile whose exponentials run on the FMA pipe (4 of 32;
-// larger shares measured slower: the polynomial costs more issue slots than
-// the MUFU pipe it relieves).
-__device__ __forceinline__ constexpr bool exp_on_fma(int pair) { return (pair & 7) == 7; }
-
 // One softmax step over a 64-key tile for this thread's row.
 //   taddr     TMEM address (lane and first column) of the 64 score columns
-//   kind      0: fp32 scores (FP16 route)   1: int32 scores (INT8 route)
+//   kind      0: FP16 route (fp16 or fp32 scores, by kNumerics)   1: INT8 route (int32 scores)
 //   ss        fp32 value of the fp16 score scale (INT8 route)
 //   lim       number of valid keys of this row in the tile (>= 64: none masked)
 //   thr       rescale threshold (0 = reference rule)
 // Outputs the packed fp16 P row in p[32]; o_scale/need_rescale say whether the
 // O accumulator row has to be multiplied by o_scale before this P is added.
-// The row maximum is taken over the fp32 values before their fp16 rounding:
-// rounding to nearest is monotonic, so fp16(max v) = max fp16(v).
+// The scores are rounded to fp16 first (the reference's qk is an fp16 tile)
+// and the row maximum is taken over the fp16 pairs. Every exponential runs on
+// ex2.approx, as tl.math.exp2 does on the GPU.
 //   brow      optional additive bias of this row and tile (element i at
 //             brow[i * bstride]): qk = fp16(qk + fp16(b * fp16(log2 e))) on the
 //             valid keys (tilemix.py:264-272, :413-421)
+template <int kNumerics>
 __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss, int lim, float thr,
                                              float& m_used, float& l, uint32_t (&p)[32], float& o_scale,
                                              bool& need_rescale, const __half* brow = nullptr,
@@ -160,25 +118,37 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss,
   tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
   tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
   tmem_wait_ld();
-  if (kind != 0) {
-    // f32(i) * ss in one rounding: with a = float(i + 0x4B400000) = 1.5*2^23 + i,
-    // fma(a, ss, -1.5*2^23*ss) evaluates a*ss - 1.5*2^23*ss = i*ss exactly before
-    // its single rounding (-1.5*2^23*ss is exact: ss has an 11-bit significand).
-    const float c = -12582912.0f * ss;
-    const uint64_t ss2 = f32x2_pack(ss, ss), c2 = f32x2_pack(c, c);
+  // qk of the row as fp16 pairs: h[i] = (qk[2i], qk[2i+1]).
+  uint32_t h[32];
+  if (kNumerics == kNumericsGpu && kind == 0) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const uint64_t a2 = f32x2_pack(__uint_as_float(s[2 * i] + 0x4B400000u), __uint_as_float(s[2 * i + 1] + 0x4B400000u));
-      const float2 v = f32x2_unpack(f32x2_fma(a2, ss2, c2));
-      s[2 * i] = __float_as_uint(v.x);
-      s[2 * i + 1] = __float_as_uint(v.y);
+    for (int i = 0; i < 32; ++i) h[i] = __byte_perm(s[2 * i], s[2 * i + 1], 0x5410);
+  } else {
+    if (kind != 0) {
+      // f32(i) * ss in one rounding: with a = float(i + 0x4B400000) = 1.5*2^23 + i,
+      // fma(a, ss, -1.5*2^23*ss) evaluates a*ss - 1.5*2^23*ss = i*ss exactly before
+      // its single rounding (-1.5*2^23*ss is exact: ss has an 11-bit significand).
+      const float c = -12582912.0f * ss;
+      const uint64_t ss2 = f32x2_pack(ss, ss), c2 = f32x2_pack(c, c);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint64_t a2 = f32x2_pack(__uint_as_float(s[2 * i] + 0x4B400000u), __uint_as_float(s[2 * i + 1] + 0x4B400000u));
+        const float2 v = f32x2_unpack(f32x2_fma(a2, ss2, c2));
+        s[2 * i] = __float_as_uint(v.x);
+        s[2 * i + 1] = __float_as_uint(v.y);
+      }
     }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) h[i] = pack_half2_rn(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]));
   }
-  const float kNegInf = -__int_as_float(0x7f800000);
   if (__any_sync(0xffffffffu, lim < kKeys)) {
 #pragma unroll
-    for (int i = 0; i < 64; ++i)
-      if (i >= lim) s[i] = 0xFF800000u;  // -inf
+    for (int i = 0; i < 32; ++i) {
+      if (2 * i >= lim)
+        h[i] = 0xFC00FC00u;  // (-inf, -inf)
+      else if (2 * i + 1 >= lim)
+        h[i] = (h[i] & 0xFFFFu) | 0xFC000000u;
+    }
   }
   if (brow != nullptr) {
     // fp16 products and sums, each rounded once: fp32 holds the exact product
@@ -190,24 +160,25 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss,
       if (i < lim) {
         const float b = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(brow) + i * bstride)));
         const float bb = __half2float(__float2half_rn(b * l2e));
-        const float q16 = __half2float(__float2half_rn(__uint_as_float(s[i])));
-        s[i] = __float_as_uint(__half2float(__float2half_rn(q16 + bb)));
+        const uint32_t hw = h[i >> 1];
+        const float q16 = __half2float(__ushort_as_half(static_cast<unsigned short>((i & 1) ? hw >> 16 : hw & 0xFFFFu)));
+        const uint32_t r = __half_as_ushort(__float2half_rn(q16 + bb));
+        h[i >> 1] = (i & 1) ? ((hw & 0xFFFFu) | (r << 16)) : ((hw & 0xFFFF0000u) | r);
       }
     }
   }
-  // Row maximum: a tree of 3-input maxima (64 -> 22 -> 8 -> 4 -> 2 -> 1).
-  float m1[22];
+  // Row maximum over the fp16 pairs (a tree of packed maxima), then of the two halves.
+  uint32_t m16[16];
 #pragma unroll
-  for (int i = 0; i < 21; ++i)
-    m1[i] = max3f(__uint_as_float(s[3 * i]), __uint_as_float(s[3 * i + 1]), __uint_as_float(s[3 * i + 2]));
-  m1[21] = __uint_as_float(s[63]);
-  float m2[8];
+  for (int i = 0; i < 16; ++i) m16[i] = hmax2_u32(h[2 * i], h[2 * i + 1]);
 #pragma unroll
-  for (int i = 0; i < 7; ++i) m2[i] = max3f(m1[3 * i], m1[3 * i + 1], m1[3 * i + 2]);
-  m2[7] = m1[21];
-  const float m3a = max3f(m2[0], m2[1], m2[2]), m3b = max3f(m2[3], m2[4], m2[5]);
-  const float mraw = max3f(m3a, m3b, fmaxf(m2[6], m2[7]));
-  const float mx = __half2float(__float2half_rn(mraw));
+  for (int w = 8; w >= 1; w >>= 1) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) m16[i] = hmax2_u32(m16[i], m16[i + w]);
+  }
+  const uint32_t mm = hmax2_u32(m16[0], __byte_perm(m16[0], 0u, 0x1032));
+  const float kNegInf = -__int_as_float(0x7f800000);
+  const float mx = __half2float(__ushort_as_half(static_cast<unsigned short>(mm & 0xFFFFu)));
   const bool has = mx != kNegInf;
   o_scale = 1.f;
   need_rescale = false;
@@ -215,43 +186,30 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss,
     const float alpha = ex2_approx(m_used - mx);  // 0 when m_used == -inf
     need_rescale = (m_used != kNegInf);
     o_scale = alpha;
-    l *= alpha;
     m_used = mx;
   }
   if (has) {
-    // l accumulates the exponentials before their fp16 rounding (two packed
-    // partial sums); the rounding of p stays exactly the reference's.
+    // p = fp16(exp2(f32(qk) - m)), qk - m by the mixed-precision add (one
+    // rounding, as fp16 - fp32 promotes to fp32); l sums the rounded p in fp32.
     const float negm = -m_used;
-    // Lower clamp for the FMA-pipe pairs: x >= floor16(m_used - 120) - m_used
-    // keeps floor(x) >= -126; every clamped weight is below 2^-120, which is 0
-    // in fp16 and below the resolution of l.
-    uint32_t lo2;
-    {
-      const float lo = fmaxf(m_used - 120.f, -65504.f);
-      uint16_t lh;
-      asm("cvt.rp.f16.f32 %0, %1;" : "=h"(lh) : "f"(lo));
-      lo2 = static_cast<uint32_t>(lh) * 0x10001u;
-    }
-    uint64_t acc0 = 0, acc1 = 0;
+    float la = 0.f, lb = 0.f, lc = 0.f, ld = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      uint32_t h2 = pack_half2_rn(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]));
-      float e0, e1;
-      if (exp_on_fma(i)) {
-        h2 = hmax2_u32(h2, lo2);
-        exp2_poly_x2(add_f32_f16_lo(h2, negm), add_f32_f16_hi(h2, negm), e0, e1);
-      } else {
-        e0 = ex2_approx(add_f32_f16_lo(h2, negm));
-        e1 = ex2_approx(add_f32_f16_hi(h2, negm));
-      }
-      if (i & 1)
-        acc1 = f32x2_add(acc1, f32x2_pack(e0, e1));
-      else
-        acc0 = f32x2_add(acc0, f32x2_pack(e0, e1));
+      const float e0 = ex2_approx(add_f32_f16_lo(h[i], negm));
+      const float e1 = ex2_approx(add_f32_f16_hi(h[i], negm));
       p[i] = pack_half2_rn(e0, e1);
+      if (i & 1) {
+        lc = add_f32_f16_lo(p[i], lc);
+        ld = add_f32_f16_hi(p[i], ld);
+      } else {
+        la = add_f32_f16_lo(p[i], la);
+        lb = add_f32_f16_hi(p[i], lb);
+      }
     }
-    const float2 a0 = f32x2_unpack(acc0), a1 = f32x2_unpack(acc1);
-    l += (a0.x + a0.y) + (a1.x + a1.y);
+    // l = l * alpha + l_tile: one FMA on the GPU (the reference's compiler
+    // contracts it), a rounded product and a rounded sum in exact numerics.
+    const float lt = (la + lb) + (lc + ld);
+    l = kNumerics == kNumericsGpu ? fmaf(l, o_scale, lt) : __fadd_rn(__fmul_rn(l, o_scale), lt);
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i) p[i] = 0u;
@@ -282,8 +240,9 @@ __device__ __forceinline__ void rescale_o_row(uint32_t taddr, float scale) {
   }
 }
 
-// Normalise this thread's O row (D fp32 columns in TMEM) by l and store it as fp16.
-template <int D>
+// Normalise this thread's O row (D fp32 columns in TMEM) by l and store it as
+// fp16 (the division of the numerics, common.cuh normalize_pair).
+template <int kNumerics, int D>
 __device__ __forceinline__ void store_o_row(uint32_t taddr, bool have_o, float l, __half* orow, bool store) {
 #pragma unroll 1
   for (int c = 0; c < D; c += 32) {
@@ -296,17 +255,11 @@ __device__ __forceinline__ void store_o_row(uint32_t taddr, bool have_o, float l
       for (int i = 0; i < 32; ++i) o[i] = 0u;
     }
     if (store) {
-      // acc / l: reciprocal once per row, then per element one residual
-      // correction (Markstein's method: q0 = a*r, e = a - q0*l, q = q0 + e*r),
-      // which gives the correctly rounded quotient for these normal operands.
       const float rl = __frcp_rn(l);
       uint32_t w[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float a0 = __uint_as_float(o[2 * i]), a1 = __uint_as_float(o[2 * i + 1]);
-        const float q0 = a0 * rl, q1 = a1 * rl;
-        w[i] = pack_half2_rn(fmaf(fmaf(-q0, l, a0), rl, q0), fmaf(fmaf(-q1, l, a1), rl, q1));
-      }
+      for (int i = 0; i < 16; ++i)
+        w[i] = normalize_pair<kNumerics>(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]), l, rl);
       uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
       for (int v = 0; v < 4; ++v) dst[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);

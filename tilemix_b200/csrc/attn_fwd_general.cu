@@ -151,7 +151,7 @@ __device__ __forceinline__ void convert_v8_stage(uint8_t* smem, int s, int t) {
   }
 }
 
-template <int D>
+template <int kNumerics, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     tilemix_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_k16, const __grid_constant__ CUtensorMap tm_k8,
                             const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_v8,
@@ -256,7 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 5) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc_qk16 = make_idesc(1, 0, 0, 0, 128, 64);
+      // FP16 scores accumulate in fp16 (GPU numerics) or fp32 (exact numerics).
+      const uint32_t idesc_qk16 = make_idesc(kNumerics == kNumericsGpu ? 0 : 1, 0, 0, 0, 128, 64);
       const uint32_t idesc_qk8 = make_idesc(2, 1, 0, 0, 128, 64);
       const uint32_t idesc_pv = make_idesc(1, 0, 0, 1, 128, static_cast<uint32_t>(D));
       const uint32_t k8_layout = (D == 128) ? 2u : 4u;
@@ -368,25 +369,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) bars->red[warp] = m;
           named_bar_sync_softmax();
           m = fmaxf(fmaxf(bars->red[0], bars->red[1]), fmaxf(bars->red[2], bars->red[3]));
-          const float scale = __fdiv_rn(m, 127.f);
-          const float rscale = __frcp_rn(scale);
+          const float scale = quant_scale<kNumerics>(m);
+          // a zero or non-finite block scale quantises to zeros, as in the reference
+          const bool finite = scale > 0.f && scale <= 3.4028235e38f;
+          QuantDiv qd;
+          qd.init(scale);
           sq16 = __float2half_rn(scale);
 #pragma unroll
           for (int c8 = 0; c8 < D / 8; ++c8) {
             const __half2* h = reinterpret_cast<const __half2*>(&raw[c8]);
-            uint32_t w0 = 0, w1 = 0;
+            uint32_t u[8];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 f = __half22float2(h[e]);
-              const uint32_t pr = (static_cast<uint32_t>(quant_code_rcp(f.x, scale, rscale)) & 0xFFu) |
-                                  ((static_cast<uint32_t>(quant_code_rcp(f.y, scale, rscale)) & 0xFFu) << 8);
-              if (e < 2)
-                w0 |= pr << (16 * e);
-              else
-                w1 |= pr << (16 * (e - 2));
+              quant_code_pair<kNumerics>(f.x, f.y, qd, &u[2 * e], &u[2 * e + 1]);
+              if (!finite) u[2 * e] = u[2 * e + 1] = 0u;
             }
-            codes[c8 * 2] = w0;
-            codes[c8 * 2 + 1] = w1;
+            codes[c8 * 2] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410);
+            codes[c8 * 2 + 1] = __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410);
           }
         } else {
           const int8_t* q8row =
@@ -455,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int lim = seqlen_k - j * kKeys;
         if (a.causal) lim = min(lim, row + coff + 1 - j * kKeys);
         const __half* brow = brow0 ? brow0 + static_cast<int64_t>(j) * kKeys * a.b_sn : nullptr;
-        softmax_tile(tbase + lane_off + src_col, kind, ss, lim, a.rescale_threshold, m_used, l, p, o_scale,
+        softmax_tile<kNumerics>(tbase + lane_off + src_col, kind, ss, lim, a.rescale_threshold, m_used, l, p, o_scale,
                      need_rescale, brow, a.b_sn);
         if (kind == 1 && a.v8_path) {
           // p_scaled = fp16(p * sv), sv the V scale of the tile's block (:472-480)
@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[jj % kSlots], (jj / kSlots) & 1, a.err, kErrTimeoutPV));
       tc_fence_after();
     }
-    store_o_row<D>(tbase + lane_off + kColO, n_tiles > 0, l, orow, row_ok && ok);
+    store_o_row<kNumerics, D>(tbase + lane_off + kColO, n_tiles > 0, l, orow, row_ok && ok);
   }
 
   __syncwarp();
@@ -537,18 +537,25 @@ int launch_attn_general(const CUtensorMap& k16, const CUtensorMap& k8, const CUt
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TM_ERR_LAUNCH;
   static bool attr_set[64] = {};
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(tilemix_attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
-        cudaFuncSetAttribute(tilemix_attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes)) != cudaSuccess)
+    const int sm = static_cast<int>(kSmemBytes);
+    const auto attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    if (cudaFuncSetAttribute(tilemix_attn_fwd_kernel<kNumericsGpu, 64>, attr, sm) != cudaSuccess ||
+        cudaFuncSetAttribute(tilemix_attn_fwd_kernel<kNumericsGpu, 128>, attr, sm) != cudaSuccess ||
+        cudaFuncSetAttribute(tilemix_attn_fwd_kernel<kNumericsExact, 64>, attr, sm) != cudaSuccess ||
+        cudaFuncSetAttribute(tilemix_attn_fwd_kernel<kNumericsExact, 128>, attr, sm) != cudaSuccess)
       return TM_ERR_LAUNCH;
     attr_set[dev] = true;
   }
   dim3 grid(tiles, heads_q, batch);
-  if (a.D == 128)
-    tilemix_attn_fwd_kernel<128><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, v8, a);
+  const bool gpu = a.numerics == kNumericsGpu;
+  if (a.D == 128 && gpu)
+    tilemix_attn_fwd_kernel<kNumericsGpu, 128><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, v8, a);
+  else if (a.D == 128)
+    tilemix_attn_fwd_kernel<kNumericsExact, 128><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, v8, a);
+  else if (gpu)
+    tilemix_attn_fwd_kernel<kNumericsGpu, 64><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, v8, a);
   else
-    tilemix_attn_fwd_kernel<64><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, v8, a);
+    tilemix_attn_fwd_kernel<kNumericsExact, 64><<<grid, kThreads, kSmemBytes, stream>>>(k16, k8, v, v8, a);
   return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
 }
 

@@ -207,9 +207,10 @@ __device__ __forceinline__ uint32_t col_s(int x, int slot) {
 // the block scale is the maximum over the 128 rows (named barrier 1 + x over
 // the tile's 128 threads). Two passes over shared memory (absmax, then codes
 // and scaling) keep a few registers live instead of the whole row, and the
-// codes come from FMA-pipe arithmetic (quant_code_pair_fma), which leaves the
+// codes are rounded with FMA-pipe arithmetic (quant_code_pair), which leaves the
 // conversion pipe to the other tile's softmax exponentials. Returns the fp16
 // block scale.
+template <int kNumerics>
 __device__ __forceinline__ __half transform_q(uint8_t* smem, Barriers* bars, const AttnArgs& a, int x, int t,
                                               int warp, int lane, bool row_ok) {
   uint8_t* q16 = smem + kOffQ16 + x * kQ16Bytes;
@@ -254,12 +255,12 @@ __device__ __forceinline__ __half transform_q(uint8_t* smem, Barriers* bars, con
   // The reduction words are reused by the next item: nobody may overwrite
   // them before all four warps have read them.
   asm volatile("bar.sync %0, 128;" ::"r"(1 + x) : "memory");
-  const float scale = __fdiv_rn(m, 127.f);
-  const float rscale = __frcp_rn(scale);
+  const float scale = quant_scale<kNumerics>(m);
   // A zero block (scale 0) or one holding inf (scale inf) quantises to all
   // zeros in the reference (x / scale is 0 or NaN, and NaN truncates to 0).
   const bool finite = scale > 0.f && scale <= 3.4028235e38f;
-  const uint64_t r2 = f32x2_pack(rscale, rscale), ns2 = f32x2_pack(-scale, -scale);
+  QuantDiv qd;
+  qd.init(scale);
   uint8_t* q8 = smem + kOffQ8 + x * kQ8Bytes;
 #pragma unroll 4
   for (int g = 0; g < 8; ++g) {
@@ -271,7 +272,7 @@ __device__ __forceinline__ __half transform_q(uint8_t* smem, Barriers* bars, con
     for (int p = 0; p < 8; ++p) {
       const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hw[p]));
       if (finite) {
-        quant_code_pair_fma(f.x, f.y, r2, ns2, &u[2 * p], &u[2 * p + 1]);
+        quant_code_pair<kNumerics>(f.x, f.y, qd, &u[2 * p], &u[2 * p + 1]);
       } else {
         u[2 * p] = 0u;
         u[2 * p + 1] = 0u;
@@ -298,6 +299,7 @@ __device__ __forceinline__ __half transform_q(uint8_t* smem, Barriers* bars, con
 // correctly rounded quotient for these normal operands. Each thread writes its
 // own row (rows are a token stride apart), 32 bytes per store where the layout
 // allows.
+template <int kNumerics>
 __device__ __forceinline__ void epilogue_o_row(uint32_t taddr, bool have_o, float l, __half* orow, bool store,
                                                bool vec32, uint64_t* o_free) {
   const float rl = __frcp_rn(l);
@@ -325,11 +327,15 @@ __device__ __forceinline__ void epilogue_o_row(uint32_t taddr, bool have_o, floa
       uint32_t w[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const uint64_t a2 = f32x2_pack(__uint_as_float(o[2 * e]), __uint_as_float(o[2 * e + 1]));
-        const uint64_t q0 = f32x2_fma(a2, rl2, 0ull);
-        const uint64_t r = f32x2_fma(q0, nl2, a2);
-        const float2 q = f32x2_unpack(f32x2_fma(r, rl2, q0));
-        w[e] = pack_half2_rn(q.x, q.y);
+        if (kNumerics == kNumericsGpu) {
+          w[e] = normalize_pair<kNumerics>(__uint_as_float(o[2 * e]), __uint_as_float(o[2 * e + 1]), l, rl);
+        } else {
+          const uint64_t a2 = f32x2_pack(__uint_as_float(o[2 * e]), __uint_as_float(o[2 * e + 1]));
+          const uint64_t q0 = f32x2_fma(a2, rl2, 0ull);
+          const uint64_t r = f32x2_fma(q0, nl2, a2);
+          const float2 q = f32x2_unpack(f32x2_fma(r, rl2, q0));
+          w[e] = pack_half2_rn(q.x, q.y);
+        }
       }
       if (vec32) {
         asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst + 2 * c), "r"(w[0]),
@@ -343,6 +349,7 @@ __device__ __forceinline__ void epilogue_o_row(uint32_t taddr, bool have_o, floa
   }
 }
 
+template <int kNumerics>
 __global__ void __launch_bounds__(kThreads, 1)
     tilemix_attn_fwd_paired_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k16,
                                    const __grid_constant__ CUtensorMap tm_k8, const __grid_constant__ CUtensorMap tm_v,
@@ -486,7 +493,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // offset is added as offset >> 4 to the start-address field (all
     // shared-memory offsets here are < 256 KB).
     const int x = warp == 9 ? 0 : 1;
-    constexpr uint32_t idesc_qk16 = make_idesc(1, 0, 0, 0, 128, 64);
+    // FP16 scores accumulate in fp16 (GPU numerics) or fp32 (exact numerics).
+    constexpr uint32_t idesc_qk16 = make_idesc(kNumerics == kNumericsGpu ? 0 : 1, 0, 0, 0, 128, 64);
     constexpr uint32_t idesc_qk8 = make_idesc(2, 1, 0, 0, 128, 64);
     constexpr uint32_t idesc_pv = make_idesc(1, 0, 0, 1, 128, kD);
     const uint64_t dq16 = make_sdesc(smem_u32(smem + kOffQ16 + x * kQ16Bytes), 16, 1024, 2);
@@ -600,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __half sq16 = __float2half_rn(1.f);
     if (it >= 0) {
       ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_full[x], 0, a.err, kErrTimeoutQ));
-      if (tile_valid(m, x)) sq16 = transform_q(smem, bars, a, x, t, warp, lane, tile_of(m, x).mtile * kRows + t < m.seqlen_q);
+      if (tile_valid(m, x)) sq16 = transform_q<kNumerics>(smem, bars, a, x, t, warp, lane, tile_of(m, x).mtile * kRows + t < m.seqlen_q);
       mbar_arrive(&bars->q_ready[x]);
     }
     while (it >= 0 && ok) {
@@ -650,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t p[32];
         float o_scale;
         bool need_rescale;
-        softmax_tile(tbase + lane_off + col_s(x, slot), kind, ss, lim, a.rescale_threshold, m_used, l, p, o_scale,
+        softmax_tile<kNumerics>(tbase + lane_off + col_s(x, slot), kind, ss, lim, a.rescale_threshold, m_used, l, p, o_scale,
                      need_rescale);
         // P goes out first; its store overlaps the wait for the previous PV
         // when O has to be rescaled (PV(c-1) must have accumulated into O).
@@ -678,7 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_full[x], (n + 1) & 1, a.err, kErrTimeoutQ));
         if (!ok) break;
         if (tile_valid(mn, x))
-          sq16_next = transform_q(smem, bars, a, x, t, warp, lane, tile_of(mn, x).mtile * kRows + t < mn.seqlen_q);
+          sq16_next = transform_q<kNumerics>(smem, bars, a, x, t, warp, lane, tile_of(mn, x).mtile * kRows + t < mn.seqlen_q);
         mbar_arrive(&bars->q_ready[x]);
       }
       // This item's O.
@@ -687,7 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->pv_done[x][cl & 1], (cl >> 1) & 1, a.err, kErrTimeoutPV));
         tc_fence_after();
       }
-      epilogue_o_row(tbase + lane_off + col_o(x), nb > 0 && ok, l, orow, store && ok, a.o_vec32 != 0,
+      epilogue_o_row<kNumerics>(tbase + lane_off + col_o(x), nb > 0 && ok, l, orow, store && ok, a.o_vec32 != 0,
                      &bars->o_free[x]);
       sq16 = sq16_next;
       ++n;
@@ -716,8 +724,10 @@ int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUten
   static bool attr_set[64] = {};
   static int n_sm[64] = {};
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes)) != cudaSuccess)
+    if (cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel<kNumericsGpu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel<kNumericsExact>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) != cudaSuccess)
       return TM_ERR_LAUNCH;
     if (cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm[dev] <= 0)
       return TM_ERR_LAUNCH;
@@ -736,7 +746,10 @@ int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUten
   const int ctas = static_cast<int>(std::min<int64_t>(items, n_sm[dev]));
   // Long units (at least two grids' worth of levels): one unit's levels per round.
   g.chunk = g.nx >= 2 * ctas ? ctas : 1;
-  tilemix_attn_fwd_paired_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(q, k16, k8, v, a, g);
+  if (a.numerics == kNumericsGpu)
+    tilemix_attn_fwd_paired_kernel<kNumericsGpu><<<ctas, kThreads, kSmemBytes, stream>>>(q, k16, k8, v, a, g);
+  else
+    tilemix_attn_fwd_paired_kernel<kNumericsExact><<<ctas, kThreads, kSmemBytes, stream>>>(q, k16, k8, v, a, g);
   return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
 }
 

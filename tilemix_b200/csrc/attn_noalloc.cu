@@ -5,21 +5,28 @@
 // The entry point allocates nothing: no cudaMalloc / cudaFree and no library
 // call that allocates.
 //
-// Scratch capacity (device memory reserved when the library is loaded):
+// Scratch capacity (device memory the module holds on every device where it is
+// loaded; under CUDA's lazy module loading that happens at the latest when the
+// first call on the device resolves the scratch address):
 //   K codes   16 MiB  -> k_tokens * heads_k * head_dim <= 16,777,216
 //   K scales  512 KiB -> (k_tokens / blkk + batch) * heads_k <= 262,144
 //   offsets   256 KiB -> batch + 1 <= 65,536
-// Larger problems are rejected with TM_ERR_UNSUPPORTED before anything runs.
-// Every scratch word a call reads is written earlier in the same call on the
-// same stream (the offsets by prefix_blocks_kernel, codes and scales by the
-// quantiser), so nothing has to start at zero. Calls that can be in flight at
-// the same time (other streams, other host threads) share the scratch and race.
+// Larger problems are rejected with TM_ERR_UNSUPPORTED, and every argument is
+// checked (tm_attn_fwd_ex's checks, with the scratch standing in for the K
+// operand) before anything is queued on the stream. Every scratch word a call
+// reads is written earlier in the same call on the same stream (the offsets by
+// prefix_blocks_kernel, codes and scales by the quantiser), so nothing has to
+// start at zero. Calls that can be in flight at the same time (other streams,
+// other host threads) share the scratch and race.
 #include <mutex>
 
 #include "common.cuh"
 #include "tilemix_b200.h"
 
 namespace tilemix {
+
+int check_attn_args(const tm_attn_params* p, const tm_attn_tuning* tuning);
+
 namespace noalloc {
 
 constexpr int64_t kMaxK8Bytes = 16ll << 20;
@@ -83,8 +90,9 @@ extern "C" int tm_attn_fwd_noalloc(const tm_attn_params* p, const tm_attn_tuning
   if (p->k == nullptr || p->cu_seqlens_k == nullptr) return TM_ERR_NULL;
   if (p->batch < 0 || p->heads_k <= 0 || p->k_tokens < 0 || (p->head_dim != 64 && p->head_dim != 128))
     return TM_ERR_SHAPE;
-  if (p->blkk <= 0 || p->blkk % 64 != 0) return TM_ERR_UNSUPPORTED;
-  if (p->batch == 0 || p->max_seqlen_q == 0) return TM_OK;
+  if (p->blkk != 64 && p->blkk != 128) return TM_ERR_UNSUPPORTED;
+  const int numerics = tuning ? tuning->numerics : TM_NUMERICS_GPU;
+  if (numerics != TM_NUMERICS_GPU && numerics != TM_NUMERICS_EXACT) return TM_ERR_SHAPE;
   const int64_t codes = p->k_tokens * p->heads_k * static_cast<int64_t>(p->head_dim);
   const int64_t scale_rows = p->k_tokens / p->blkk + p->batch;  // >= sum_b ceil(T_b / blkk)
   if (codes > kMaxK8Bytes || scale_rows * p->heads_k > kMaxScales || p->batch + 1 > kMaxOffsets)
@@ -93,19 +101,22 @@ extern "C" int tm_attn_fwd_noalloc(const tm_attn_params* p, const tm_attn_tuning
   Scratch s;
   int rc = scratch_for_current_device(&s);
   if (rc != TM_OK) return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  prefix_blocks_kernel<<<1, 32, 0, st>>>(p->cu_seqlens_k, p->batch, p->blkk, s.cu_k_scale);
-  if (cudaGetLastError() != cudaSuccess) return TM_ERR_LAUNCH;
   const int64_t k8_st = static_cast<int64_t>(p->heads_k) * p->head_dim;
-  rc = tm_quant_per_block_int8(p->k, p->k_stride_tok, p->k_stride_head, p->cu_seqlens_k, s.cu_k_scale, p->batch,
-                               p->heads_k, p->head_dim, p->blkk, p->max_seqlen_k, 1.0f, s.k8, k8_st, p->head_dim,
-                               nullptr, s.k_scale, stream);
-  if (rc != TM_OK) return rc;
   tm_attn_params q = *p;
   q.k8 = s.k8;
   q.k8_stride_tok = k8_st;
   q.k8_stride_head = p->head_dim;
   q.k_scale = s.k_scale;
   q.cu_k_scale = s.cu_k_scale;
+  rc = tilemix::check_attn_args(&q, tuning);
+  if (rc != TM_OK) return rc;
+  if (p->batch == 0 || p->max_seqlen_q == 0) return TM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  prefix_blocks_kernel<<<1, 32, 0, st>>>(p->cu_seqlens_k, p->batch, p->blkk, s.cu_k_scale);
+  if (cudaGetLastError() != cudaSuccess) return TM_ERR_LAUNCH;
+  rc = tm_quant_per_block_int8_ex(p->k, p->k_stride_tok, p->k_stride_head, p->cu_seqlens_k, s.cu_k_scale, p->batch,
+                                  p->heads_k, p->head_dim, p->blkk, p->max_seqlen_k, 1.0f, s.k8, k8_st, p->head_dim,
+                                  nullptr, s.k_scale, numerics, stream);
+  if (rc != TM_OK) return rc;
   return tm_attn_fwd_ex(&q, tuning, stream);
 }

@@ -414,46 +414,54 @@ __device__ __forceinline__ uint32_t pack_half2_rn(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// ----------------------------------------------------------------------------
+// Numerics of the reference's divisions and score accumulation
+// ----------------------------------------------------------------------------
+// The reference's kernels are Triton code. On the GPU, Triton compiles an fp32
+// `a / b` to PTX div.full.f32 (a full-range approximate division, <= 2 ulp)
+// and tl.dot(fp16, fp16, out_dtype=fp16) to tcgen05 MMAs with an fp16
+// accumulator; its interpreter (and the reference algorithm read as exact
+// arithmetic) divides with IEEE rounding and accumulates in fp32 before one
+// rounding. The kernels here take the mode as a template argument:
+//   kNumericsGpu   = the reference as it runs on the GPU (the default)
+//   kNumericsExact = the reference's algorithm with IEEE division and fp32
+//                    score accumulation (bit-exact with its interpreter run)
+enum : int { kNumericsGpu = 0, kNumericsExact = 1 };
+
+// PTX div.full.f32: the division the reference's Triton kernels execute.
+__device__ __forceinline__ float div_full(float a, float b) {
+  float r;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// scale = absmax / 127 of a quantisation block in the given numerics.
+template <int kNumerics>
+__device__ __forceinline__ float quant_scale(float absmax) {
+  return kNumerics == kNumericsGpu ? div_full(absmax, 127.f) : __fdiv_rn(absmax, 127.f);
+}
+
 // Symmetric per-block INT8 code of x for a given block scale, as the reference
-// quantiser computes it: y = x / scale (IEEE), y += (y >= 0 ? 0.5 : -0.5),
-// truncate toward zero (NaN -> 0).
+// quantiser computes it: y = x / scale, y += (y >= 0 ? 0.5 : -0.5), truncate
+// toward zero (NaN -> 0).
+template <int kNumerics>
 __device__ __forceinline__ int quant_code(float x, float scale) {
-  float y = __fdiv_rn(x, scale);
+  float y = kNumerics == kNumericsGpu ? div_full(x, scale) : __fdiv_rn(x, scale);
   y = __fadd_rn(y, y >= 0.f ? 0.5f : -0.5f);
   return __float2int_rz(y);
 }
 
-// quant_code with the quotient formed from the block's correctly rounded
-// reciprocal rcp = 1/scale and one FMA residual correction (Markstein):
-// q0 = x*rcp, q = q0 + (x - q0*scale)*rcp. For every finite fp16 x and every
-// scale = fp16 magnitude / 127 this equals the IEEE quotient x / scale (checked
-// exhaustively on a B200), except that x = -0 gives +0, which yields the same code.
-__device__ __forceinline__ int quant_code_rcp(float x, float scale, float rcp) {
-  const float q0 = x * rcp;
-  float y = fmaf(fmaf(-q0, scale, x), rcp, q0);
-  y = __fadd_rn(y, y >= 0.f ? 0.5f : -0.5f);
-  return __float2int_rz(y);
-}
-
-// Codes of a pair of x for a block scale, as quant_code_rcp but without the
-// conversion pipe (cvt.rzi shares the pipe with the softmax's ex2): the same
-// Markstein quotient y (on f32x2 pairs), then round half away from zero as
-// trunc(|y| + 0.5) with the sign of y restored. |y| + 0.5 equals the
-// reference's |y + (y >= 0 ? 0.5 : -0.5)| (round to nearest is symmetric); an
-// add rounded toward zero against 1.5 * 2^23 truncates it (it is >= 0 and
-// < 2^22), and adding 1.5 * 2^23 to the signed code leaves the code's two's
-// complement byte in the low mantissa bits. Requires a finite scale > 0
-// (callers treat other scales separately); x finite (a NaN x yields an
-// unspecified code instead of the reference's 0). Returns the low bytes of
-// the two codes in bits 0-7 of *c0 / *c1 (upper bits unspecified).
-__device__ __forceinline__ void quant_code_pair_fma(float x0, float x1, uint64_t r2, uint64_t nscale2, uint32_t* c0,
-                                                    uint32_t* c1) {
+// Round half away from zero of a pair of quotients y, on the FMA pipe (a
+// cvt.rzi would share the conversion pipe with the softmax's ex2): trunc(|y| +
+// 0.5) with the sign of y restored. |y| + 0.5 equals the reference's |y + (y >=
+// 0 ? 0.5 : -0.5)| (round to nearest is symmetric); an add rounded toward zero
+// against 1.5 * 2^23 truncates it (it is >= 0 and < 2^22), and adding 1.5 *
+// 2^23 to the signed code leaves the code's two's complement byte in the low
+// mantissa bits. Returns the low bytes of the two codes in bits 0-7 of *c0 /
+// *c1 (upper bits unspecified). |y| < 2^22 required (quotients of a block's
+// values by its scale are at most 127 in magnitude).
+__device__ __forceinline__ void round_codes_pair_fma(uint64_t y, uint32_t* c0, uint32_t* c1) {
   constexpr uint64_t kMagic2 = 0x4B4000004B400000ull;  // (1.5 * 2^23, 1.5 * 2^23)
-  const uint64_t x2 = (static_cast<uint64_t>(__float_as_uint(x1)) << 32) | __float_as_uint(x0);
-  uint64_t q0, e, y;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(q0) : "l"(x2), "l"(r2));
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(e) : "l"(q0), "l"(nscale2), "l"(x2));
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(y) : "l"(e), "l"(r2), "l"(q0));
   const float y0 = __uint_as_float(static_cast<uint32_t>(y)), y1 = __uint_as_float(static_cast<uint32_t>(y >> 32));
   const float b0 = __fadd_rn(fabsf(y0), 0.5f), b1 = __fadd_rn(fabsf(y1), 0.5f);
   const uint64_t b2 = (static_cast<uint64_t>(__float_as_uint(b1)) << 32) | __float_as_uint(b0);
@@ -467,6 +475,54 @@ __device__ __forceinline__ void quant_code_pair_fma(float x0, float x1, uint64_t
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(u) : "l"(ks), "l"(kMagic2));
   *c0 = static_cast<uint32_t>(u);
   *c1 = static_cast<uint32_t>(u >> 32);
+}
+
+// Per-block division constants of the quantiser for one block scale.
+struct QuantDiv {
+  float scale;
+  uint64_t r2;   // (1/scale, 1/scale), correctly rounded (exact numerics)
+  uint64_t ns2;  // (-scale, -scale)
+  __device__ __forceinline__ void init(float s) {
+    scale = s;
+    const float r = __frcp_rn(s);
+    r2 = (static_cast<uint64_t>(__float_as_uint(r)) << 32) | __float_as_uint(r);
+    ns2 = (static_cast<uint64_t>(__float_as_uint(-s)) << 32) | __float_as_uint(-s);
+  }
+};
+
+// Codes of a pair of x for a block scale: the quotient of the numerics, then
+// the FMA-pipe rounding above. Exact numerics form the IEEE quotient from the
+// correctly rounded reciprocal with one FMA residual correction (Markstein:
+// q0 = x*r, q = q0 + (x - q0*scale)*r); for every finite fp16 x and every
+// scale = fp16 magnitude / 127 it equals x / scale (checked exhaustively on a
+// B200), except that x = -0 gives +0, which yields the same code. GPU
+// numerics divide with div.full.f32. Requires a finite scale > 0 (callers
+// treat other scales separately) and finite x (a NaN x yields an unspecified
+// code instead of the reference's 0).
+template <int kNumerics>
+__device__ __forceinline__ void quant_code_pair(float x0, float x1, const QuantDiv& d, uint32_t* c0, uint32_t* c1) {
+  uint64_t y;
+  if (kNumerics == kNumericsGpu) {
+    y = (static_cast<uint64_t>(__float_as_uint(div_full(x1, d.scale))) << 32) | __float_as_uint(div_full(x0, d.scale));
+  } else {
+    const uint64_t x2 = (static_cast<uint64_t>(__float_as_uint(x1)) << 32) | __float_as_uint(x0);
+    uint64_t q0, e;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(q0) : "l"(x2), "l"(d.r2));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(e) : "l"(q0), "l"(d.ns2), "l"(x2));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(y) : "l"(e), "l"(d.r2), "l"(q0));
+  }
+  round_codes_pair_fma(y, c0, c1);
+}
+
+// fp16(acc / l) of a pair of fp32 accumulator values in the given numerics:
+// div.full.f32 as the reference's kernel divides on the GPU, or the correctly
+// rounded quotient (reciprocal rl = 1/l once per row, then per element one
+// residual correction: q0 = a*rl, e = a - q0*l, q = q0 + e*rl).
+template <int kNumerics>
+__device__ __forceinline__ uint32_t normalize_pair(float a0, float a1, float l, float rl) {
+  if (kNumerics == kNumericsGpu) return pack_half2_rn(div_full(a0, l), div_full(a1, l));
+  const float q0 = a0 * rl, q1 = a1 * rl;
+  return pack_half2_rn(fmaf(fmaf(-q0, l, a0), rl, q0), fmaf(fmaf(-q1, l, a1), rl, q1));
 }
 
 }  // namespace tilemix

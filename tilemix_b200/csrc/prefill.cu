@@ -89,9 +89,9 @@ constexpr int kQuantThreads = 256;
 // One CTA per (sequence, KV head, block of blk tokens): RoPE of the block's K
 // rows, then the block's per-head INT8 quantisation of the rotated values
 // (quant_per_block_varlen.py:6-45 with sm_scale 1: scale = absmax / 127 in
-// fp32, code = trunc(x / scale + 0.5 * sign), with the IEEE quotient), so the
-// attention's K quantiser need not read K again.
-template <int D, int BLK>
+// fp32, code = trunc(x / scale + 0.5 * sign), with the division of the
+// numerics, common.cuh), so the attention's K quantiser need not read K again.
+template <int kNumerics, int D, int BLK>
 __global__ void __launch_bounds__(kQuantThreads) rope_quant_kernel(const RopeQuantArgs q) {
   constexpr int kGroups = D / 16;
   constexpr int kUnits = BLK * kGroups / kQuantThreads;  // (row, group) units per thread
@@ -132,8 +132,10 @@ __global__ void __launch_bounds__(kQuantThreads) rope_quant_kernel(const RopeQua
   float m = red[0];
 #pragma unroll
   for (int w = 1; w < kQuantThreads / 32; ++w) m = fmaxf(m, red[w]);
-  const float scale = __fdiv_rn(m, 127.f);
-  const float rscale = __frcp_rn(scale);
+  const float scale = quant_scale<kNumerics>(m);
+  const bool finite = scale > 0.f && scale <= 3.4028235e38f;
+  QuantDiv qd;
+  qd.init(scale);
   const int nblk = (a.T + BLK - 1) / BLK;
   if (threadIdx.x == 0) {
     const int64_t si = (static_cast<int64_t>(b) * nblk + blk_idx) * a.H + h;
@@ -148,11 +150,21 @@ __global__ void __launch_bounds__(kQuantThreads) rope_quant_kernel(const RopeQua
     if (t >= a.T) continue;
     const unsigned short* v0 = reinterpret_cast<const unsigned short*>(&ol[k]);
     const unsigned short* v1 = reinterpret_cast<const unsigned short*>(&oh[k]);
-    uint32_t w0[2] = {0u, 0u}, w1[2] = {0u, 0u};
+    uint32_t u0[8], u1[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      w0[e >> 2] |= (static_cast<uint32_t>(quant_code_rcp(h2f(v0[e]), scale, rscale)) & 0xFFu) << (8 * (e & 3));
-      w1[e >> 2] |= (static_cast<uint32_t>(quant_code_rcp(h2f(v1[e]), scale, rscale)) & 0xFFu) << (8 * (e & 3));
+    for (int e = 0; e < 8; e += 2) {
+      quant_code_pair<kNumerics>(h2f(v0[e]), h2f(v0[e + 1]), qd, &u0[e], &u0[e + 1]);
+      quant_code_pair<kNumerics>(h2f(v1[e]), h2f(v1[e + 1]), qd, &u1[e], &u1[e + 1]);
+    }
+    uint32_t w0[2], w1[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      w0[i] = finite ? __byte_perm(__byte_perm(u0[4 * i], u0[4 * i + 1], 0x0040),
+                                   __byte_perm(u0[4 * i + 2], u0[4 * i + 3], 0x0040), 0x5410)
+                     : 0u;
+      w1[i] = finite ? __byte_perm(__byte_perm(u1[4 * i], u1[4 * i + 1], 0x0040),
+                                   __byte_perm(u1[4 * i + 2], u1[4 * i + 3], 0x0040), 0x5410)
+                     : 0u;
     }
     int8_t* k8 = q.k8 + ((static_cast<int64_t>(b) * a.T + t) * a.H + h) * D + 8 * u;
     *reinterpret_cast<uint2*>(k8) = make_uint2(w0[0], w0[1]);
@@ -255,7 +267,8 @@ extern "C" int tm_rotary_token_major(const void* q, int64_t q_sb, int64_t q_sh, 
                                      int64_t k_sb, int64_t k_sh, int64_t k_st, const void* cos, int64_t cos_sb,
                                      int64_t cos_st, const void* sin, int64_t sin_sb, int64_t sin_st, int batch,
                                      int heads_q, int heads_k, int seq_len, int head_dim, void* oq, void* ok,
-                                     int8_t* k8, void* k_scale_f16, float* k_scale_f32, int blkk, void* stream) {
+                                     int8_t* k8, void* k_scale_f16, float* k_scale_f32, int blkk, int numerics,
+                                     void* stream) {
   if (!q || !k || !cos || !sin || !oq || !ok) return TM_ERR_NULL;
   if (batch < 0 || heads_q <= 0 || heads_k <= 0 || seq_len < 0) return TM_ERR_SHAPE;
   if (head_dim != 64 && head_dim != 128) return TM_ERR_UNSUPPORTED;
@@ -269,6 +282,7 @@ extern "C" int tm_rotary_token_major(const void* q, int64_t q_sb, int64_t q_sh, 
   for (int64_t s : strides)
     if (s % 8 != 0) return TM_ERR_ALIGN;
   if (k8 && blkk != 64 && blkk != 128) return TM_ERR_UNSUPPORTED;
+  if (numerics != TM_NUMERICS_GPU && numerics != TM_NUMERICS_EXACT) return TM_ERR_SHAPE;
   if (k8 && !aligned16p(k8)) return TM_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   RopeArgs qa{static_cast<const __half*>(q), q_sb, q_sh, q_st, static_cast<const __half*>(cos),
@@ -289,14 +303,21 @@ extern "C" int tm_rotary_token_major(const void* q, int64_t q_sb, int64_t q_sh, 
   } else {
     RopeQuantArgs qq{ka, k8, static_cast<__half*>(k_scale_f16), k_scale_f32, blkk};
     const dim3 grid((seq_len + blkk - 1) / blkk, heads_k, batch);
+    using tilemix::kNumericsExact;
+    using tilemix::kNumericsGpu;
+    const bool gpu = numerics == TM_NUMERICS_GPU;
     if (head_dim == 128 && blkk == 64)
-      rope_quant_kernel<128, 64><<<grid, kQuantThreads, 0, st>>>(qq);
+      gpu ? rope_quant_kernel<kNumericsGpu, 128, 64><<<grid, kQuantThreads, 0, st>>>(qq)
+          : rope_quant_kernel<kNumericsExact, 128, 64><<<grid, kQuantThreads, 0, st>>>(qq);
     else if (head_dim == 128)
-      rope_quant_kernel<128, 128><<<grid, kQuantThreads, 0, st>>>(qq);
+      gpu ? rope_quant_kernel<kNumericsGpu, 128, 128><<<grid, kQuantThreads, 0, st>>>(qq)
+          : rope_quant_kernel<kNumericsExact, 128, 128><<<grid, kQuantThreads, 0, st>>>(qq);
     else if (blkk == 64)
-      rope_quant_kernel<64, 64><<<grid, kQuantThreads, 0, st>>>(qq);
+      gpu ? rope_quant_kernel<kNumericsGpu, 64, 64><<<grid, kQuantThreads, 0, st>>>(qq)
+          : rope_quant_kernel<kNumericsExact, 64, 64><<<grid, kQuantThreads, 0, st>>>(qq);
     else
-      rope_quant_kernel<64, 128><<<grid, kQuantThreads, 0, st>>>(qq);
+      gpu ? rope_quant_kernel<kNumericsGpu, 64, 128><<<grid, kQuantThreads, 0, st>>>(qq)
+          : rope_quant_kernel<kNumericsExact, 64, 128><<<grid, kQuantThreads, 0, st>>>(qq);
   }
   return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
 }

@@ -33,6 +33,7 @@ __device__ __forceinline__ float block_absmax_reduce(float v, float* red) {
   return m;
 }
 
+template <int kNumerics>
 __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_kernel(
     const __half* __restrict__ x, int64_t x_stride_tok, int64_t x_stride_head, const int32_t* __restrict__ cu_seqlens,
     const int32_t* __restrict__ cu_scale, int heads, int dim, int blk, float sm_scale, int8_t* __restrict__ out,
@@ -81,7 +82,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_kernel(
     }
   }
   amax = block_absmax_reduce(amax, red);
-  const float scale = __fdiv_rn(amax, 127.f);
+  const float scale = quant_scale<kNumerics>(amax);
 
   auto quant_vec = [&](const uint4& u) -> uint2 {
     const __half2* h = reinterpret_cast<const __half2*>(&u);
@@ -89,8 +90,8 @@ __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_kernel(
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       float2 f = __half22float2(h[e]);
-      const uint32_t a = static_cast<uint32_t>(quant_code(f.x * sm_scale, scale)) & 0xFFu;
-      const uint32_t b = static_cast<uint32_t>(quant_code(f.y * sm_scale, scale)) & 0xFFu;
+      const uint32_t a = static_cast<uint32_t>(quant_code<kNumerics>(f.x * sm_scale, scale)) & 0xFFu;
+      const uint32_t b = static_cast<uint32_t>(quant_code<kNumerics>(f.y * sm_scale, scale)) & 0xFFu;
       const uint32_t pair = a | (b << 8);
       if (e < 2)
         lo |= pair << (16 * e);
@@ -126,11 +127,13 @@ __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_kernel(
 // The same quantisation for sm_scale == 1, head dims 64 / 128 and blocks of
 // 64 / 128 tokens: the case of every K (and V) the attention quantises. Sizes
 // are compile-time (no per-vector division), the block stays in registers, and
-// the codes come from quant_code_pair_fma: exact here because every |x| of a
-// block is at most its absmax m, an fp16 value, with scale = m / 127 (checked
-// against the reference rounding for all such pairs). A block whose scale is 0
-// or not finite quantises to zeros and a NaN value to 0, as in the reference.
-template <int DIM, int BLK>
+// the codes come from quant_code_pair (the quotient of the numerics, rounded on
+// the FMA pipe; exact numerics' Markstein quotient is the IEEE one here because
+// every |x| of a block is at most its absmax m, an fp16 value, with scale =
+// m / 127, checked against the reference rounding for all such pairs). A block
+// whose scale is 0 or not finite quantises to zeros and a NaN value to 0, as in
+// the reference.
+template <int kNumerics, int DIM, int BLK>
 __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_unit_kernel(
     const __half* __restrict__ x, int64_t x_stride_tok, int64_t x_stride_head, const int32_t* __restrict__ cu_seqlens,
     const int32_t* __restrict__ cu_scale, int heads, int8_t* __restrict__ out, int64_t o_stride_tok,
@@ -161,12 +164,10 @@ __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_unit_kerne
   }
   const float2 amf = __half22float2(*reinterpret_cast<const __half2*>(&am2));
   const float amax = block_absmax_reduce(fmaxf(amf.x, amf.y), red);
-  const float scale = __fdiv_rn(amax, 127.f);
-  const float rscale = __frcp_rn(scale);
+  const float scale = quant_scale<kNumerics>(amax);
   const bool finite = scale > 0.f && scale <= 3.4028235e38f;
-  uint64_t r2, ns2;
-  r2 = (static_cast<uint64_t>(__float_as_uint(rscale)) << 32) | __float_as_uint(rscale);
-  ns2 = (static_cast<uint64_t>(__float_as_uint(-scale)) << 32) | __float_as_uint(-scale);
+  QuantDiv qd;
+  qd.init(scale);
 #pragma unroll
   for (int i = 0; i < kVecs; ++i) {
     const int r = i * (kQuantThreads / kVecPerRow) + threadIdx.x / kVecPerRow;
@@ -177,7 +178,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_unit_kerne
     for (int e = 0; e < 4; ++e) {
       const float2 f = __half22float2(h[e]);
       if (finite) {
-        quant_code_pair_fma(f.x, f.y, r2, ns2, &u[2 * e], &u[2 * e + 1]);
+        quant_code_pair<kNumerics>(f.x, f.y, qd, &u[2 * e], &u[2 * e + 1]);
         if (f.x != f.x) u[2 * e] = 0u;  // NaN truncates to 0 in the reference
         if (f.y != f.y) u[2 * e + 1] = 0u;
       } else {
@@ -198,13 +199,47 @@ __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_unit_kerne
 
 }  // namespace tilemix
 
-extern "C" int tm_quant_per_block_int8(const void* x, int64_t x_stride_tok, int64_t x_stride_head,
-                                       const int32_t* cu_seqlens, const int32_t* cu_scale, int batch, int heads,
-                                       int dim, int blk, int max_seqlen, float sm_scale, int8_t* out,
-                                       int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32,
-                                       void* scale_f16, void* stream) {
+namespace {
+
+template <int kNumerics>
+int launch_quant(const void* x, int64_t x_stride_tok, int64_t x_stride_head, const int32_t* cu_seqlens,
+                 const int32_t* cu_scale, int heads, int dim, int blk, float sm_scale, int8_t* out,
+                 int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32, void* scale_f16, dim3 grid,
+                 cudaStream_t st) {
+  using namespace tilemix;
+  const __half* xh = static_cast<const __half*>(x);
+  __half* s16 = static_cast<__half*>(scale_f16);
+  if (sm_scale == 1.0f && (dim == 64 || dim == 128) && (blk == 64 || blk == 128)) {
+    if (dim == 128 && blk == 64)
+      quant_per_block_int8_unit_kernel<kNumerics, 128, 64><<<grid, kQuantThreads, 0, st>>>(
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+    else if (dim == 128)
+      quant_per_block_int8_unit_kernel<kNumerics, 128, 128><<<grid, kQuantThreads, 0, st>>>(
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+    else if (blk == 64)
+      quant_per_block_int8_unit_kernel<kNumerics, 64, 64><<<grid, kQuantThreads, 0, st>>>(
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+    else
+      quant_per_block_int8_unit_kernel<kNumerics, 64, 128><<<grid, kQuantThreads, 0, st>>>(
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+  } else {
+    quant_per_block_int8_kernel<kNumerics><<<grid, kQuantThreads, 0, st>>>(
+        xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, dim, blk, sm_scale, out, out_stride_tok,
+        out_stride_head, scale_f32, s16);
+  }
+  return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
+}
+
+}  // namespace
+
+extern "C" int tm_quant_per_block_int8_ex(const void* x, int64_t x_stride_tok, int64_t x_stride_head,
+                                          const int32_t* cu_seqlens, const int32_t* cu_scale, int batch, int heads,
+                                          int dim, int blk, int max_seqlen, float sm_scale, int8_t* out,
+                                          int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32,
+                                          void* scale_f16, int numerics, void* stream) {
   if (x == nullptr || out == nullptr || cu_seqlens == nullptr || cu_scale == nullptr) return TM_ERR_NULL;
   if (batch < 0 || heads <= 0 || dim <= 0 || blk <= 0 || max_seqlen < 0) return TM_ERR_SHAPE;
+  if (numerics != TM_NUMERICS_GPU && numerics != TM_NUMERICS_EXACT) return TM_ERR_SHAPE;
   if ((dim & 7) != 0) return TM_ERR_SHAPE;
   if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0 || (x_stride_tok & 7) != 0 || (x_stride_head & 7) != 0)
     return TM_ERR_ALIGN;
@@ -215,27 +250,21 @@ extern "C" int tm_quant_per_block_int8(const void* x, int64_t x_stride_tok, int6
   if (heads > 65535 || batch > 65535) return TM_ERR_SHAPE;
   dim3 grid(nblk, heads, batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (sm_scale == 1.0f && (dim == 64 || dim == 128) && (blk == 64 || blk == 128)) {
-    using namespace tilemix;
-    const __half* xh = static_cast<const __half*>(x);
-    __half* s16 = static_cast<__half*>(scale_f16);
-    if (dim == 128 && blk == 64)
-      quant_per_block_int8_unit_kernel<128, 64><<<grid, kQuantThreads, 0, st>>>(
-          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
-    else if (dim == 128)
-      quant_per_block_int8_unit_kernel<128, 128><<<grid, kQuantThreads, 0, st>>>(
-          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
-    else if (blk == 64)
-      quant_per_block_int8_unit_kernel<64, 64><<<grid, kQuantThreads, 0, st>>>(
-          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
-    else
-      quant_per_block_int8_unit_kernel<64, 128><<<grid, kQuantThreads, 0, st>>>(
-          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
-    return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
-  }
-  tilemix::quant_per_block_int8_kernel<<<grid, tilemix::kQuantThreads, 0, st>>>(
-      static_cast<const __half*>(x), x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, dim, blk, sm_scale,
-      out, out_stride_tok, out_stride_head, scale_f32, static_cast<__half*>(scale_f16));
-  const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
+  if (numerics == TM_NUMERICS_GPU)
+    return launch_quant<tilemix::kNumericsGpu>(x, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, dim, blk,
+                                                sm_scale, out, out_stride_tok, out_stride_head, scale_f32, scale_f16,
+                                                grid, st);
+  return launch_quant<tilemix::kNumericsExact>(x, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, dim, blk,
+                                                sm_scale, out, out_stride_tok, out_stride_head, scale_f32, scale_f16,
+                                                grid, st);
+}
+
+extern "C" int tm_quant_per_block_int8(const void* x, int64_t x_stride_tok, int64_t x_stride_head,
+                                       const int32_t* cu_seqlens, const int32_t* cu_scale, int batch, int heads,
+                                       int dim, int blk, int max_seqlen, float sm_scale, int8_t* out,
+                                       int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32,
+                                       void* scale_f16, void* stream) {
+  return tm_quant_per_block_int8_ex(x, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, batch, heads, dim, blk,
+                                    max_seqlen, sm_scale, out, out_stride_tok, out_stride_head, scale_f32, scale_f16,
+                                    TM_NUMERICS_GPU, stream);
 }

@@ -137,7 +137,7 @@ def _rotary_args(q: Tensor, k: Tensor, cos: Tensor, sin: Tensor):
 def _launch_rotary(q, k, cos, sin, oq, ok, k8=None, k_scale=None, blkk=64):
     import ctypes
 
-    from tilemix_b200._lib import check, lib
+    from tilemix_b200._lib import check, lib, numerics_code
 
     b, hq, hk, t, d = _rotary_args(q, k, cos, sin)
     cb = cos.stride(0) if cos.shape[0] > 1 else 0
@@ -147,7 +147,7 @@ def _launch_rotary(q, k, cos, sin, oq, ok, k8=None, k_scale=None, blkk=64):
         rc = lib().tm_rotary_token_major(ptr(q), q.stride(0), q.stride(1), q.stride(2), ptr(k), k.stride(0),
                                          k.stride(1), k.stride(2), ptr(cos), cb, cos.stride(1), ptr(sin), sb,
                                          sin.stride(1), b, hq, hk, t, d, ptr(oq), ptr(ok), ptr(k8), ptr(k_scale),
-                                         ctypes.c_void_p(0), blkk, _stream(q))
+                                         ctypes.c_void_p(0), blkk, numerics_code(), _stream(q))
     check(rc, "tm_rotary_token_major")
 
 

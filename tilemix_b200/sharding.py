@@ -22,6 +22,35 @@ from typing import Callable, Optional, Sequence
 import torch
 
 
+def kv_head_block(heads_k: int, world_size: int, rank: int) -> Optional[tuple[int, int]]:
+    """The contiguous KV heads [h0, h1) of ``rank`` when the world size divides the KV heads:
+    the rank then owns the units (every sequence) x [h0, h1), an equal share of any batch,
+    and its inputs and outputs are strided views of the full packed tensors (no packing, no
+    scatter). None when the world size does not divide the KV heads (use ``plan_units``)."""
+    if world_size < 1 or not 0 <= rank < world_size:
+        raise ValueError("rank must lie in [0, world_size)")
+    if heads_k % world_size:
+        return None
+    per = heads_k // world_size
+    return rank * per, (rank + 1) * per
+
+
+def head_block_views(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+                     precision_map: torch.Tensor, m_blocks: int, block: tuple[int, int]):
+    """Views of one KV-head block [h0, h1) of packed [tokens, heads, D] q / k / v / out and
+    its routing words (rows h * m_blocks + [0, m_blocks) for h in the block, contiguous).
+
+    Exact for batches of equal sequence length m_blocks * block_m >= T > (m_blocks - 1) *
+    block_m: the kernels index the words of KV head h with the sequence's own block count
+    (attention/triton/tilemix.py:819-823), which is then m_blocks for every sequence. Varlen
+    batches shard with ``plan_units`` / ``sharded_attention``, which group units by the words
+    they read."""
+    h0, h1 = block
+    g = q.shape[1] // k.shape[1]
+    return (q[:, h0 * g:h1 * g], k[:, h0:h1], v[:, h0:h1], out[:, h0 * g:h1 * g],
+            precision_map[h0 * m_blocks:h1 * m_blocks])
+
+
 def unit_cost(length: int, group: int, causal: bool = True) -> int:
     return group * (length * (length + 1) // 2 if causal else length * length)
 
