@@ -11,15 +11,18 @@ forward over the batch: per-block INT8 quantisation of K, then the fused
 attention kernel (Q is quantised inside it); the routing map is built once
 beforehand, as the model integration caches it.
 
-One process per GPU (torchrun for N > 1). Sharding is over independent
-(sequence x KV-head) units with no collective: every rank runs its own full
-batch (weak scaling) and ``value`` is the FLOPs of all ranks divided by the
-slowest rank's time. Rank 0 prints one JSON line.
+One process per GPU (torchrun for N > 1), strong scaling: the one workload's
+64 (sequence x KV-head) units are split over the ranks with no collective
+(with N dividing the 8 KV heads, rank r owns KV heads [8r/N, 8(r+1)/N) of every
+sequence and writes its output in place); ``value`` is the workload's FLOPs
+divided by the slowest rank's time. Rank 0 prints one JSON line, which at N=1
+also carries the reference's own Triton kernels timed on the same GPU and
+inputs (``triton_reference``) and the all-FP16 / all-INT8 patterns.
 
-``--impl reference`` times the CPU restatement of the reference's kernels (the
-oracle, bit-exact with the reference run under the Triton interpreter) on the
-host cores, on a bounded sample of the same workload; under torchrun only
-rank 0 runs it.
+``--impl reference`` times the reference's CPU path on the host cores: the
+CPU restatement of its kernels (the oracle, bit-exact with the reference run
+under the Triton interpreter) on a bounded sample of the same workload; under
+torchrun only rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -42,9 +45,14 @@ UNIT = "TFLOP/s"
 CFG = dict(batch=8, seq_len=4096, heads_q=24, heads_k=8, head_dim=128, outliers=4, outlier_scale=20.0,
            pattern="sptrans", percentage=0.5, block_m=128, block_n=64, block_n_mask=64)
 FALLBACK_PEAKS = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
+# The reference's own CPU path is its Triton kernels under TRITON_INTERPRET=1; measured on one
+# unit of this workload (3 Q heads / 1 KV head, T = 4096, sptrans 50 %) it ran at this rate.
+INTERPRETER_NOTE = ("the reference's kernels under TRITON_INTERPRET=1 ran one (sequence, KV-head) unit of this "
+                    "workload (3 Q heads, T = 4096) in 50.8 s on one core: 0.254 GFLOP/s per core, about 3x "
+                    "slower per core than the port timed here")
 
 
-def config_dict(n_gpus: int) -> dict:
+def config_dict(n_gpus: int, shard: str = "") -> dict:
     c = CFG
     tokens = c["batch"] * c["seq_len"]
     rd = tokens * (c["heads_q"] + 2 * c["heads_k"]) * c["head_dim"] * 2
@@ -55,10 +63,10 @@ def config_dict(n_gpus: int) -> dict:
         "batch": c["batch"], "seq_len": c["seq_len"], "heads_q": c["heads_q"], "heads_k": c["heads_k"],
         "head_dim": c["head_dim"], "pattern": c["pattern"], "int8_percentage": c["percentage"],
         "block_m": c["block_m"], "block_n": c["block_n"], "block_n_mask": c["block_n_mask"],
-        "parallelism": f"shard{n_gpus}: every GPU runs its own batch of {c['batch'] * c['heads_k']} "
-                       "(sequence x KV-head) units, no collective",
+        "parallelism": f"shard{n_gpus}: the {c['batch'] * c['heads_k']} (sequence x KV-head) units of the one "
+                       f"workload split over {n_gpus} GPU(s), no collective" + (f"; rank 0: {shard}" if shard else ""),
         "l2": f"inputs larger than L2 (126 MB): each step reads Q, K, V ({rd / 1e6:.0f} MB) and writes O and K8 "
-              f"({wr / 1e6:.0f} MB); no flush",
+              f"({wr / 1e6:.0f} MB) over all ranks; no flush",
     }
 
 
@@ -169,7 +177,7 @@ class ClockSampler:
             "sm_max_mhz": max(r[2] for r in used) if used else None,
             "reasons": reasons,
             "samples": len(used),
-            "window": "timed region" if inside else "whole run (no sample inside the timed region)",
+            "window": "run-up + timed region" if inside else "whole run (no sample inside the timed region)",
         }
 
 
@@ -252,7 +260,7 @@ def run_reference(args) -> None:
     value = flops / step_s / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "fp16+int8", "data": "synthetic (seeded N(0,1) with outlier channels)",
         "config": config_dict(args.gpus), "impl": "reference",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
@@ -272,6 +280,135 @@ def run_unit_proxy():
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+def make_problems(q, k, v, o, cu, words, rank: int, world: int):
+    """This rank's share of the workload as launches over views of the resident tensors.
+
+    Units are (sequence x KV-head) pairs; every one is independent, so no data crosses
+    ranks. When the world size divides the KV heads a rank owns a contiguous KV-head block
+    of every sequence: its Q/K/V/O are strided views of the full tensors and its output
+    lands in place. Otherwise units are dealt longest-processing-time first
+    (tilemix_b200/sharding.py) and packed into one single-KV-head problem before the timed
+    region; its output then has to be scattered back (timed separately)."""
+    import torch
+
+    from tilemix_b200.sharding import head_block_views, kv_head_block, pack_units, plan_units
+
+    c = CFG
+    B, T, HQ, HK, bm = c["batch"], c["seq_len"], c["heads_q"], c["heads_k"], c["block_m"]
+    g = HQ // HK
+    mb = (T + bm - 1) // bm
+    hb = kv_head_block(HK, world, rank)
+    if hb is not None:
+        h0, h1 = hb
+        pm_all = words.view(torch.int64).repeat(HK).view(torch.uint64)
+        qv, kv, vv, ov, pm = head_block_views(q, k, v, o, pm_all, mb, hb)
+        return [dict(q=qv, k=kv, v=vv, o=ov, cu=cu, T=T, pm=pm,
+                     units=[(b, h) for b in range(B) for h in range(h0, h1)])], \
+            f"kv-head block [{h0}, {h1}) of every sequence (views, output in place)"
+    units = plan_units([T] * B, HK, world, g)[rank]
+    cu_list = [i * T for i in range(B + 1)]
+    q_r, k_r, v_r, cu_r, _ = pack_units(q, k, v, cu_list, units)
+    # every KV head reads the same routing words in this workload (the map is head-independent)
+    return [dict(q=q_r, k=k_r, v=v_r, o=torch.empty_like(q_r), cu=cu_r, T=T, pm=words, units=units,
+                 packed=True)], f"{len(units)} (sequence x KV-head) units dealt longest first, packed"
+
+
+def problem_flops(p) -> float:
+    c = CFG
+    g = c["heads_q"] // c["heads_k"]
+    T = c["seq_len"]
+    return float(4 * c["head_dim"] * g * len(p["units"]) * T * (T + 1) // 2)
+
+
+def measure_int8_peak(dev) -> dict:
+    """Dense INT8 tensor throughput of this GPU: torch._int_mm (cuBLASLt) on 8192^3, best of 10."""
+    import torch
+
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev).t().contiguous().t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    del a, b
+    return {"int8_tops": 2 * n ** 3 / (best * 1e-3) / 1e12, "how": "torch._int_mm int8 8192^3 -> int32, best of 10"}
+
+
+def triton_reference_leg(q, k, v, cu, pm_by_pattern: dict, steps: int, warmup: int) -> dict:
+    """The reference's own Triton implementation on this GPU (unmodified, from baseline/_ref):
+    tilemix_attention_with_quant (Q and K quantisation + attn_fwd) with the configuration its
+    prefill benchmark forces (TILEMIX_FORCE_CONFIG=128,64,8,2,0), timed with CUDA events like
+    our step, beside the same call through this package's drop-in API on the same inputs, and
+    the largest / mean absolute difference of the two outputs."""
+    import torch
+
+    ref_root = REPO / "baseline" / "_ref"
+    if not (ref_root / "attention" / "triton" / "tilemix.py").exists():
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    if str(ref_root) not in sys.path:
+        sys.path.append(str(ref_root))
+    os.environ["TILEMIX_FORCE_CONFIG"] = "128,64,8,2,0"
+    try:
+        from attention.triton.tilemix import tilemix_attention_with_quant as ref_call
+    except Exception as e:  # noqa: BLE001 - report, do not fail the bench line
+        return {"unavailable": f"importing the reference failed: {type(e).__name__}: {e}"}
+    from tilemix_b200.attention.tilemix import tilemix_attention_with_quant as our_call
+
+    c = CFG
+    T = c["seq_len"]
+    flops = attention_flops()
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    out = {"impl": "reference Triton kernels (attention/triton/tilemix.py:1340-1447, unmodified) on this GPU",
+           "config": "TILEMIX_FORCE_CONFIG=128,64,8,2,0 (BLOCK_M 128, BLOCK_N 64, 8 warps, 2 stages)",
+           "step": "tilemix_attention_with_quant: Q and K quantisation + attn_fwd", "patterns": {}}
+    cases = [(name, pm, mode, True) for name, (pm, mode) in pm_by_pattern.items()]
+    cases.append(("sptrans, int8_use_fp16_v=False (the API default)", pm_by_pattern["sptrans"][0], "mixed", False))
+    for name, pm, mode, fp16_v in cases:
+        kw = dict(block_m=c["block_m"], block_n=c["block_n"], block_n_mask=c["block_n_mask"], causal=True,
+                  routing_mode=mode, scalar_scales=True, int8_use_fp16_v=fp16_v)
+        try:
+            o_ref, _ = ref_call(q, k, v, cu, cu, T, T, pm, **kw)
+            ms_ref = timed(lambda: ref_call(q, k, v, cu, cu, T, T, pm, **kw))
+        except Exception as e:  # noqa: BLE001
+            out["patterns"][name] = {"unavailable": f"{type(e).__name__}: {e}"}
+            continue
+        o_ours, _ = our_call(q, k, v, cu, cu, T, T, pm, **kw)
+        ms_ours = timed(lambda: our_call(q, k, v, cu, cu, T, T, pm, **kw))
+        d = (o_ours.float() - o_ref.float()).abs()
+        out["patterns"][name] = {
+            "triton_ms": ms_ref, "triton_tflops": flops / (ms_ref * 1e-3) / 1e12,
+            "ours_same_api_ms": ms_ours, "ours_same_api_tflops": flops / (ms_ours * 1e-3) / 1e12,
+            "speedup": ms_ref / ms_ours,
+            "max_abs_diff": float(d.max()), "mean_abs_diff": float(d.mean()),
+            "bit_identical_share": float((d == 0).float().mean()),
+        }
+        del o_ref, o_ours, d
+    sp = out["patterns"].get("sptrans", {})
+    out["ms"] = sp.get("triton_ms")
+    out["ratio_ours_over_triton"] = sp.get("speedup")
+    return out
+
+
 def run_ours(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -290,6 +427,7 @@ def run_ours(args) -> None:
     from tilemix_b200.attention import tilemix as tmx
     from tilemix_b200.attention.precision_maps import make_precision_bitmask
     from tilemix_b200.attention.tilemix_varlen import tilemix_varlen_attention_from_host
+    from tilemix_b200.sharding import unpack_units
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -311,64 +449,128 @@ def run_ours(args) -> None:
     c = CFG
     B, T, HQ, HK, D = c["batch"], c["seq_len"], c["heads_q"], c["heads_k"], c["head_dim"]
     bm, bn, bnm = c["block_m"], c["block_n"], c["block_n_mask"]
-    q_cpu, k_cpu, v_cpu = make_inputs(rank)
+    # The whole workload, identical on every rank; each rank computes only its shard.
+    q_cpu, k_cpu, v_cpu = make_inputs(0)
     q, k, v = q_cpu.to(dev), k_cpu.to(dev), v_cpu.to(dev)
-    words = make_precision_bitmask(T, bm, bnm, None, c["percentage"], c["pattern"], {"percentage": c["percentage"]},
-                                   bn, device=dev)
-    pm = words.view(torch.int64).repeat(HK).view(torch.uint64)
-    words_host = [int(x) for x in words.view(torch.int64).cpu().numpy().view("uint64")]
-    share = int8_share(words_host, bm, bn, bnm, T)
     cu = torch.arange(0, (B + 1) * T, T, device=dev, dtype=torch.int32)
     o = torch.empty_like(q)
     sm_scale = D ** -0.5
     thr = tmx.rescale_threshold()
-    scalar = bm == 128 and bn == 64
 
-    def step(ev_a=None, ev_b=None):
-        k8, sk16, cuks = tmx._quantize_k(k, cu, T, 64, equal_len=T)
-        if ev_a is not None:
-            ev_a.record()
-        tmx._launch(q, k, v, o, cu, cu, pm, T, T, k8=k8, sk=sk16, cuks=cuks, block_m=bm, block_n=bn,
-                    block_n_mask=bnm, BLKQ=128, BLKK=64, causal=True, sm_scale=sm_scale,
-                    mode_code=tmx.ROUTING_MODE_MIXED, scalar_scales=scalar, int8_use_fp16_v=True, threshold=thr)
-        if ev_b is not None:
-            ev_b.record()
+    def pattern_words(pattern):
+        params = {"percentage": c["percentage"]} if pattern not in ("zero", "one") else {}
+        return make_precision_bitmask(T, bm, bnm, None, c["percentage"], pattern, params, bn, device=dev)
 
+    words = pattern_words(c["pattern"])
+    words_host = [int(x) for x in words.view(torch.int64).cpu().numpy().view("uint64")]
+    share = int8_share(words_host, bm, bn, bnm, T)
+    problems, shard_desc = make_problems(q, k, v, o, cu, words, rank, world)
+    rank_flops = sum(problem_flops(p) for p in problems)
+    total_flops = attention_flops()
+
+    def make_step(probs, pm_key, mode_code):
+        def step(evs=None):
+            for i, p in enumerate(probs):
+                k8 = sk16 = cuks = None
+                if mode_code != tmx.ROUTING_MODE_FP16:
+                    k8, sk16, cuks = tmx._quantize_k(p["k"], p["cu"], p["T"], 64, equal_len=p["T"])
+                if evs is not None:
+                    evs[i][0].record()
+                tmx._launch(p["q"], p["k"], p["v"], p["o"], p["cu"], p["cu"], p[pm_key], p["T"], p["T"], k8=k8,
+                            sk=sk16, cuks=cuks, block_m=bm, block_n=bn, block_n_mask=bnm, BLKQ=128, BLKK=64,
+                            causal=True, sm_scale=sm_scale, mode_code=mode_code, scalar_scales=True,
+                            int8_use_fp16_v=True, threshold=thr)
+                if evs is not None:
+                    evs[i][1].record()
+        return step
+
+    step = make_step(problems, "pm", tmx.ROUTING_MODE_MIXED)
     for _ in range(args.warmup):
         step()
     barrier()
     if tmx.device_error_code(dev) != 0:
         raise RuntimeError("attention kernel reported a device-side timeout during warm-up")
 
-    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in problems]
+           for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(gpu_id_for(local_rank))
     sampler.start()
+    # The timed steps take milliseconds, less than the sampler's 100 ms period: the same steps
+    # run back to back for about a second right before them, untimed, so that the clock
+    # samples (window: this run-up and the timed region) see the GPU under this load.
     barrier()
     t_host0 = time.time()
+    while time.time() - t_host0 < 1.0:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+    barrier()
     start.record()
     for i in range(args.steps):
-        step(ev_a[i], ev_b[i])
+        step(evs[i])
     end.record()
     barrier()
     t_host1 = time.time()
     sampler.mark(t_host0, t_host1)
     clocks = sampler.stop()
     ms_step = max_over_ranks(start.elapsed_time(end) / args.steps)
-    attn_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(ev_a, ev_b)) / args.steps)
+    attn_ms = max_over_ranks(sum(a.elapsed_time(b) for row in evs for a, b in row) / args.steps)
     if tmx.device_error_code(dev) != 0:
         raise RuntimeError("attention kernel reported a device-side timeout in the timed region")
 
-    # end to end through the public API for host-resident data: pinned host inputs in, output
-    # back to pinned host memory, every byte crossing PCIe inside the timed region (sequences
-    # are streamed, so copies in, attention and copies out overlap)
-    q_pin, k_pin, v_pin = q_cpu.pin_memory(), k_cpu.pin_memory(), v_cpu.pin_memory()
-    out_pin = torch.empty((B * T, HQ, D), dtype=torch.float16).pin_memory()
+    # the output scatter of a packed shard (not needed for KV-head blocks: they write in place)
+    scatter_ms = 0.0
+    if any(p.get("packed") for p in problems):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for p in problems:
+            unpack_units(p["o"], [i * T for i in range(B + 1)], p["units"], o)
+        e1.record()
+        barrier()
+        scatter_ms = max_over_ranks(e0.elapsed_time(e1))
+
+    # the same step with the all-FP16 and all-INT8 maps (BASELINE config 2's other patterns);
+    # the routing mode is the one routing_mode="auto" selects for them
+    pattern_lines = {"sptrans": {"ms_per_step": ms_step, "tflops": total_flops / (ms_step * 1e-3) / 1e12,
+                                 "routing_mode": "mixed"}}
+    pm_by_pattern = {"sptrans": (words.view(torch.int64).repeat(HK).view(torch.uint64), "mixed")}
+    for pattern, mode in (("zero", "fp16"), ("one", "int8")):
+        w_p = pattern_words(pattern)
+        pm_by_pattern[pattern] = (w_p.view(torch.int64).repeat(HK).view(torch.uint64), mode)
+        for p in problems:
+            p["pm_" + pattern] = w_p.view(torch.int64).repeat(p["pm"].numel() // w_p.numel()).view(torch.uint64)
+        st = make_step(problems, "pm_" + pattern, tmx._routing_mode_code(mode))
+        for _ in range(args.warmup):
+            st()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            st()
+        e1.record()
+        barrier()
+        ms_p = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        pattern_lines[pattern] = {"ms_per_step": ms_p, "tflops": total_flops / (ms_p * 1e-3) / 1e12,
+                                  "routing_mode": mode}
+    if tmx.device_error_code(dev) != 0:
+        raise RuntimeError("attention kernel reported a device-side timeout (patterns)")
+
+    # end to end through the public API for host-resident data: this rank's shard of Q, K, V
+    # in pinned host memory, its output back to pinned host memory, every byte crossing PCIe
+    # inside the timed region (sequences are streamed, so copies in, attention and copies out
+    # overlap)
+    host = []
+    for p in problems:
+        host.append(dict(q=p["q"].cpu().contiguous().pin_memory(), k=p["k"].cpu().contiguous().pin_memory(),
+                         v=p["v"].cpu().contiguous().pin_memory(),
+                         o=torch.empty(tuple(p["q"].shape), dtype=torch.float16).pin_memory(), pm=p["pm"]))
 
     def e2e_step():
-        tilemix_varlen_attention_from_host(q_pin, k_pin, v_pin, out_pin, T, bm, bn, block_n_mask=bnm, causal=True,
-                                           scale=sm_scale, precision_map_all=pm, device=dev, chunk_seqs=1, ring=2)
+        for h in host:
+            tilemix_varlen_attention_from_host(h["q"], h["k"], h["v"], h["o"], T, bm, bn, block_n_mask=bnm,
+                                               causal=True, scale=sm_scale, precision_map_all=h["pm"], device=dev,
+                                               chunk_seqs=1, ring=2)
 
     e2e_steps = max(3, min(args.steps, 30))
     for _ in range(max(3, min(args.warmup, 5))):
@@ -381,18 +583,29 @@ def run_ours(args) -> None:
     e1.record()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-    h2d = (q.numel() + k.numel() + v.numel()) * 2
-    d2h = out_pin.numel() * 2
+    h2d = sum((h["q"].numel() + h["k"].numel() + h["v"].numel()) * 2 for h in host)
+    d2h = sum(h["o"].numel() * 2 for h in host)
+    if world > 1:
+        t = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        h2d, d2h = int(t[0].item()), int(t[1].item())
+    del host
 
-    flops = attention_flops()
-    value = world * flops / (ms_step * 1e-3) / 1e12
+    value = total_flops / (ms_step * 1e-3) / 1e12
     peaks, peak_src = load_peaks()
-    peak = float(peaks["bf16_tflops"])
-    achieved = flops / (attn_ms * 1e-3) / 1e12
-    int8_peak = 2.0 * peak
-    t_star_ms = flops / 2 * (1 - share) / (peak * 1e12) * 1e3 + flops / 2 * share / (int8_peak * 1e12) * 1e3 \
-        + flops / 2 / (peak * 1e12) * 1e3
+    peak16 = float(peaks["bf16_tflops"])
+    int8 = measure_int8_peak(dev)
+    peak8 = -max_over_ranks(-int8["int8_tops"])  # the slowest GPU's
+    achieved = rank_flops / (attn_ms * 1e-3) / 1e12
+    t_star_ms = (rank_flops / 2 * (1 - share) / peak16 + rank_flops / 2 * share / peak8 + rank_flops / 2 / peak16) \
+        / 1e12 * 1e3
     traffic = profiled_traffic("attn_fwd_paired_config2")
+    if traffic is not None and world > 1:
+        traffic = int(traffic * rank_flops / total_flops)
+
+    triton_line = None
+    if world == 1 and not args.no_triton_reference:
+        triton_line = triton_reference_leg(q, k, v, cu, pm_by_pattern, min(args.steps, 20), args.warmup)
 
     cpu_line = None
     if want_cpu:
@@ -403,7 +616,7 @@ def run_ours(args) -> None:
             pool.map(run_unit_proxy(), tasks, chunksize=1)
             dt = time.perf_counter() - t0
             cpu_line = {"value": cflops / dt / 1e12, "unit": UNIT, "cores": cpu_cores, "kind": "port",
-                        "sample": sample, "seconds": dt}
+                        "sample": sample, "seconds": dt, "interpreter_note": INTERPRETER_NOTE}
         finally:
             pool.close()
             pool.join()
@@ -411,25 +624,31 @@ def run_ours(args) -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp16+int8", "data": "synthetic (seeded N(0,1) with outlier channels)",
-            "config": config_dict(world),
+            "config": config_dict(world, shard_desc),
             "roofline": {
-                "bound": "tensor", "kernel": "attn_fwd_paired", "achieved": achieved, "peak": peak,
-                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                "peak_source": f"bf16_tflops (burst) of {peak_src}", "kernel_ms": attn_ms,
-                "flops_per_launch": flops,
-                "mixed": {"int8_share": share, "int8_peak_assumed": int8_peak, "t_star_ms": t_star_ms,
-                          "frac": t_star_ms / attn_ms,
-                          "note": "routed FP16/INT8 roofline; INT8 dense peak taken as 2x the measured bf16 peak"},
+                "bound": "tensor", "kernel": "attn_fwd_paired", "achieved": achieved,
+                "peak": rank_flops / t_star_ms / 1e9, "unit": "TFLOP/s", "frac": t_star_ms / attn_ms,
+                "traffic": traffic,
+                "peak_source": f"routed FP16/INT8 mix: bf16_tflops (burst) of {peak_src} for the FP16 share and "
+                               "the INT8 GEMM peak measured in this run (torch._int_mm) for the INT8 share",
+                "kernel_ms": attn_ms, "t_star_ms": t_star_ms, "flops_per_launch": rank_flops, "int8_share": share,
+                "peak_fp16": peak16, "peak_int8": peak8, "int8_peak_measurement": int8["how"],
+                "bf16_frac": achieved / peak16,
             },
+            "patterns": pattern_lines,
+            "triton_reference": triton_line,
             "cpu_baseline": cpu_line,
-            "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "steps": e2e_steps,
-                    "api": "tilemix_varlen_attention_from_host (pinned host q/k/v/out, 1 sequence per chunk)"},
+                    "api": "tilemix_varlen_attention_from_host (pinned host q/k/v/out of each rank's shard, "
+                           "1 sequence per chunk)"},
+            "scatter_ms": scatter_ms,
             "clocks": clocks,
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 2 * len(problems) * args.steps,
             "rescale_threshold": thr,
+            "numerics": tmx.numerics_mode(),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -634,8 +853,11 @@ def run_model_prefill(args) -> None:
 
 
 VARLEN = dict(sequences=8, min_len=8192, max_len=131072, heads_q=32, heads_k=8, head_dim=128)
-VARLEN_CASES = (("sptrans", 0.5), ("band", 0.5), ("bigbird", 0.5), ("row_rand", 0.25), ("global", 0.75),
-                ("zero", None), ("one", None))
+# Config 5's grid: every percentage-driven pattern at INT8 shares 0 / 25 / 50 / 75 / 100 %, plus the
+# all-FP16 and all-INT8 maps.
+VARLEN_PCTS = (0.0, 0.25, 0.5, 0.75, 1.0)
+VARLEN_CASES = tuple((p, pct) for p in ("sptrans", "band", "global", "row_rand", "align_sparse", "bigbird")
+                     for pct in VARLEN_PCTS) + (("zero", None), ("one", None))
 
 
 def run_varlen(args) -> None:
@@ -657,7 +879,7 @@ def run_varlen(args) -> None:
     from tilemix_b200.attention import tilemix as tmx
     from tilemix_b200.attention.precision_maps import make_precision_bitmask
     from tilemix_b200.models._attention_base import pick_mask_block_n
-    from tilemix_b200.sharding import map_rows, pack_units, plan_units
+    from tilemix_b200.sharding import map_rows, pack_units, plan_units, unpack_units
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -686,33 +908,43 @@ def run_varlen(args) -> None:
         torch.cuda.synchronize()
 
     results = []
+    o_full = torch.empty_like(q) if world > 1 else None
+    steps = max(3, min(args.steps, 5))
     for pattern, pct in VARLEN_CASES:
         words = make_precision_bitmask(T_max, bm, bnm, None, pct, pattern,
                                        {"percentage": pct} if pct is not None else {}, bn, device=dev)
         pm = words.view(torch.int64).repeat(HK).view(torch.uint64)
+        pack_ms = 0.0
         if world == 1:
             cu = torch.tensor(cu_list, dtype=torch.int32, device=dev)
-            problems = [(q, k, v, cu, T_max, pm)]
+            problems = [(q, k, v, cu, T_max, pm, None)]
         else:
+            # the rank's units packed into single-KV-head problems (a gather of its Q/K/V
+            # rows), grouped by the routing words they read; timed, outside the step
             by_rows: dict = {}
             for u in units:
                 off, _ = map_rows(pm, u, lens[u[0]], bm)
                 by_rows.setdefault(off, []).append(u)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
             problems = []
             for off, us in sorted(by_rows.items()):
                 q_r, k_r, v_r, cu_r, mx = pack_units(q, k, v, cu_list, us)
-                problems.append((q_r, k_r, v_r, cu_r, mx, pm[off:off + (mx + bm - 1) // bm].contiguous()))
+                problems.append((q_r, k_r, v_r, cu_r, mx, pm[off:off + (mx + bm - 1) // bm].contiguous(), us))
+            e1.record()
+            torch.cuda.synchronize()
+            pack_ms = e0.elapsed_time(e1)
+        outs = [torch.empty_like(pr[0]) for pr in problems]
 
         def step():
-            for q_, k_, v_, cu_, mx_, pm_ in problems:
+            for (q_, k_, v_, cu_, mx_, pm_, _), o_ in zip(problems, outs):
                 tmx._attention_forward(q_, k_, v_, cu_, cu_, mx_, mx_, pm_, block_m=bm, block_n=bn, block_n_mask=bnm,
                                        BLKQ=128, BLKK=64, causal=True, sm_scale=None, mode="mixed",
-                                       scalar_scales=True, int8_use_fp16_v=True)
+                                       scalar_scales=True, int8_use_fp16_v=True, o=o_)
 
         for _ in range(2):
             step()
         barrier()
-        steps = max(3, min(args.steps, 5))
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
@@ -720,15 +952,24 @@ def run_varlen(args) -> None:
         e1.record()
         barrier()
         ms = e0.elapsed_time(e1) / steps
+        scatter_ms = 0.0
         if world > 1:
-            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            # the rank's outputs scattered back into the [tokens, HQ, D] layout (timed, outside the step)
+            e0.record()
+            for (_, _, _, _, _, _, us), o_ in zip(problems, outs):
+                unpack_units(o_, cu_list, us, o_full)
+            e1.record()
+            torch.cuda.synchronize()
+            scatter_ms = e0.elapsed_time(e1)
+            t = torch.tensor([ms, pack_ms, scatter_ms], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+            ms, pack_ms, scatter_ms = (float(x) for x in t.tolist())
         if tmx.device_error_code(dev) != 0:
             raise RuntimeError("attention kernel reported a device-side timeout")
         results.append({"pattern": pattern, "int8_percentage": pct, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12,
-                        "launches_per_step": len(problems)})
-        del problems
+                        "launches_per_step": len(problems), "pack_ms": pack_ms, "scatter_ms": scatter_ms,
+                        "tflops_with_pack_and_scatter": flops / ((ms + pack_ms + scatter_ms) * 1e-3) / 1e12})
+        del problems, outs
     if rank == 0:
         print(json.dumps({
             "component": "varlen attention (config 5)", "unit": "TFLOP/s", "n_gpus": world,
@@ -737,7 +978,9 @@ def run_varlen(args) -> None:
                                    "32 q / 8 kv heads, head_dim 128, causal", "lengths": lens,
                        "tokens": cu_list[-1], "block_m": bm, "block_n": bn, "block_n_mask": bnm,
                        "parallelism": f"shard{world}: (sequence x KV-head) units dealt longest first, no collective"},
-            "flops_per_step": flops, "steps": max(3, min(args.steps, 5)), "warmup": 2, "cases": results,
+            "flops_per_step": flops, "steps": steps, "warmup": 2, "cases": results,
+            "pack_scatter_note": "at N > 1 each rank gathers its units' Q/K/V rows into packed problems and scatters "
+                                 "its outputs back; both are timed per case outside the step (pack_ms, scatter_ms)",
         }), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
@@ -747,10 +990,12 @@ def run_varlen(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the oracle timing on the host cores")
+    ap.add_argument("--no-triton-reference", action="store_true",
+                    help="skip timing the reference's Triton kernels on the GPU (N=1 line)")
     ap.add_argument("--batch", type=int, default=CFG["batch"],
                     help="sequences per GPU (default: the workload's 8; smaller only for profiling captures)")
     ap.add_argument("--model", choices=tuple(MODEL_SPECS), default="llama3b",
