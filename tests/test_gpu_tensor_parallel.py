@@ -1,7 +1,9 @@
-"""GPU test of the head-sharded tensor parallelism on 2 GPUs (skipped with fewer): a small
-TileMix Llama prepared for prefill, sharded across two NCCL ranks, must give the last-position
-logits of the same model on one GPU (the routed attention runs per rank on its own heads;
-only the all-reduce summation order differs)."""
+"""GPU tests of the head-sharded tensor parallelism (skipped on boxes with fewer GPUs than
+ranks): a small TileMix model sharded across NCCL ranks must give the last-position logits
+of the same model on one GPU (the routed attention runs per rank on its own heads; only the
+all-reduce summation order differs). Llama on 2 ranks splits heads evenly; a Qwen2 layout
+of 14 query / 2 KV heads on 4 ranks replicates each KV head on two ranks and splits its 7
+query heads 4 + 3, the uneven split Qwen2-7B (28 / 4) takes at TP 8."""
 import os
 import socket
 
@@ -13,19 +15,31 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _model(dev):
-    from transformers import LlamaConfig, LlamaForCausalLM
+def _model(dev, kind="llama"):
+    if kind == "llama":
+        from transformers import LlamaConfig, LlamaForCausalLM
 
-    from tilemix_b200.models.tilemix_llama import (configure_tilemix_attention_pattern, inject_tilemix_into_llama,
-                                                   prepare_llama_prefill)
+        from tilemix_b200.models.tilemix_llama import (configure_tilemix_attention_pattern, inject_tilemix_into_llama,
+                                                       prepare_llama_prefill)
 
-    cfg = LlamaConfig(hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=8,
-                      num_key_value_heads=2, vocab_size=1000, max_position_embeddings=8192, rope_theta=500000.0)
+        cfg = LlamaConfig(hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=8,
+                          num_key_value_heads=2, vocab_size=1000, max_position_embeddings=8192, rope_theta=500000.0)
+        torch.manual_seed(0)
+        model = LlamaForCausalLM(cfg).to(dev, torch.float16).eval()
+        inject_tilemix_into_llama(model)
+        configure_tilemix_attention_pattern(model, "sptrans", percentage=0.5)
+        prepare_llama_prefill(model)
+        return model
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from tilemix_b200.models.tilemix_qwen import configure_tilemix_attention_pattern, inject_tilemix_into_qwen
+
+    cfg = Qwen2Config(hidden_size=896, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=14,
+                      num_key_value_heads=2, vocab_size=1000, max_position_embeddings=8192)
     torch.manual_seed(0)
-    model = LlamaForCausalLM(cfg).to(dev, torch.float16).eval()
-    inject_tilemix_into_llama(model)
-    configure_tilemix_attention_pattern(model, "sptrans", percentage=0.5)
-    prepare_llama_prefill(model)
+    model = Qwen2ForCausalLM(cfg).to(dev, torch.float16).eval()
+    inject_tilemix_into_qwen(model)
+    configure_tilemix_attention_pattern(model, "bigbird", percentage=0.5)
     return model
 
 
@@ -37,7 +51,7 @@ def _logits(model, dev):
         return model(ids, past_key_values=PrefillCache(), use_cache=True, logits_to_keep=1).logits
 
 
-def _worker(rank, world, port, path):
+def _worker(rank, world, port, path, kind):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
@@ -46,7 +60,7 @@ def _worker(rank, world, port, path):
         from tilemix_b200.attention.tilemix import device_error_code
         from tilemix_b200.models.tensor_parallel import shard_model_for_tensor_parallel
 
-        model = shard_model_for_tensor_parallel(_model(dev))
+        model = shard_model_for_tensor_parallel(_model(dev, kind))
         out = _logits(model, dev)
         torch.cuda.synchronize()
         assert device_error_code(dev) == 0
@@ -64,12 +78,13 @@ def _free_port():
 
 
 @pytest.mark.timeout(600)
-def test_two_gpu_tensor_parallel_prefill_matches_one_gpu(tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("kind,world", [("llama", 2), ("qwen", 4)])
+def test_tensor_parallel_prefill_matches_one_gpu(tmp_path, kind, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     path = str(tmp_path / "tp.pt")
-    mp.spawn(_worker, args=(2, _free_port(), path), nprocs=2, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), path, kind), nprocs=world, join=True)
     got = torch.load(path).float()
-    ref = _logits(_model(torch.device("cuda", 0)), torch.device("cuda", 0)).float().cpu()
+    ref = _logits(_model(torch.device("cuda", 0), kind), torch.device("cuda", 0)).float().cpu()
     rel = float((got - ref).norm() / ref.norm())
     assert rel < 1e-2, rel
