@@ -342,6 +342,47 @@ def measure_int8_peak(dev) -> dict:
     return {"int8_tops": 2 * n ** 3 / (best * 1e-3) / 1e12, "how": "torch._int_mm int8 8192^3 -> int32, best of 10"}
 
 
+MAP_PATTERNS = ("zero", "one", "band", "global", "row_rand", "align_sparse", "bigbird", "sptrans")
+
+
+def map_builder_leg(dev, reps: int = 50) -> dict:
+    """The routing-map kernel (``tm_build_precision_map``) for every pattern at the workload's
+    geometry (T, block_m, block_n_mask, block_n) and 50 % INT8: CUDA-event time per build over
+    ``reps`` back-to-back asynchronous launches, and the achieved HBM rate of its algorithmic
+    traffic (it reads no tensor and writes one uint64 word per query block)."""
+    import torch
+
+    from tilemix_b200.attention.precision_maps import make_precision_bitmask
+
+    c = CFG
+    T, bm, bnm, bn, pct = c["seq_len"], c["block_m"], c["block_n_mask"], c["block_n"], c["percentage"]
+    out = {}
+    for pattern in MAP_PATTERNS:
+        params = {"percentage": pct} if pattern not in ("zero", "one") else {}
+
+        def build(check=False):
+            return make_precision_bitmask(T, bm, bnm, None, pct, pattern, params, bn, device=dev, check_retarget=check)
+
+        words = build(check=True)
+        for _ in range(3):
+            build()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            build()
+        e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        nbytes = words.numel() * 8
+        out[pattern] = {"us_per_build": us, "bytes_written": nbytes, "gb_per_s": nbytes / (us * 1e-6) / 1e9}
+    return {"kernel": "build_map_kernel (tm_build_precision_map)", "seq_len": T, "block_m": bm,
+            "block_n_mask": bnm, "percentage": pct, "patterns": out,
+            "note": "one CTA per map; latency-bound by the reference's sequential retarget walk and MT19937 "
+                    "draws, not by HBM (the whole map is ceil(T / block_m) words); each time includes the "
+                    "host-side launch of its call"}
+
+
 def triton_reference_leg(q, k, v, cu, pm_by_pattern: dict, steps: int, warmup: int) -> dict:
     """The reference's own Triton implementation on this GPU (unmodified, from baseline/_ref):
     tilemix_attention_with_quant (Q and K quantisation + attn_fwd) with the configuration its
@@ -603,6 +644,7 @@ def run_ours(args) -> None:
     if traffic is not None and world > 1:
         traffic = int(traffic * rank_flops / total_flops)
 
+    map_line = map_builder_leg(dev) if world == 1 else None
     triton_line = None
     if world == 1 and not args.no_triton_reference:
         triton_line = triton_reference_leg(q, k, v, cu, pm_by_pattern, min(args.steps, 20), args.warmup)
@@ -638,6 +680,7 @@ def run_ours(args) -> None:
                 "bf16_frac": achieved / peak16,
             },
             "patterns": pattern_lines,
+            "map_builder": map_line,
             "triton_reference": triton_line,
             "cpu_baseline": cpu_line,
             "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
