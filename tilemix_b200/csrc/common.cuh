@@ -141,7 +141,7 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, i
 }
 
 // ----------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA: plain tiled loads from this GPU's own memory
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2) {
