@@ -75,6 +75,19 @@ int tm_quant_per_block_int8_ex(const void* x, int64_t x_stride_tok, int64_t x_st
                                int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32,
                                void* scale_f16, int numerics, void* stream);
 
+/* tm_quant_per_block_int8_ex with sm_scale 1 that also writes every code as
+ * an exact fp16 value to out_f16 ([tokens, heads, dim], 16-byte aligned rows):
+ * the V operand of the paired kernel's INT8-V path (tm_attn_params.v8_f16).
+ * out (the int8 codes) may be NULL. dim and blk 64 or 128, else
+ * TM_ERR_UNSUPPORTED. No reference counterpart: the reference's kernel
+ * converts the int8 V tile to fp16 as it loads it (tilemix.py:497). */
+int tm_quant_per_block_int8_f16(const void* x, int64_t x_stride_tok, int64_t x_stride_head,
+                                const int32_t* cu_seqlens, const int32_t* cu_scale, int batch, int heads,
+                                int dim, int blk, int max_seqlen, int8_t* out, int64_t out_stride_tok,
+                                int64_t out_stride_head, void* out_f16, int64_t out_f16_stride_tok,
+                                int64_t out_f16_stride_head, float* scale_f32, void* scale_f16, int numerics,
+                                void* stream);
+
 /* Routing-map patterns of make_precision_bitmask (attention/precision_maps.py:404-636). */
 #define TM_MAP_ZERO 0
 #define TM_MAP_ONE 1
@@ -158,6 +171,13 @@ typedef struct tm_attn_params {
   int64_t v8_stride_tok, v8_stride_head;
   const void* v_scale;
   const int32_t* cu_v_scale;
+  /* Optional exact fp16 copy of the v8 codes ([k_tokens, heads_k, head_dim],
+   * 16-byte rows; tm_quant_per_block_int8_f16 writes it beside the codes). With
+   * it, INT8-V calls of the paired kernel's shape (head_dim 128, block_m 128,
+   * Q quantised in kernel, no bias) run on that kernel, which loads the V
+   * operand of INT8-routed tiles from here; v8 may then be NULL. */
+  const void* v8_f16;
+  int64_t v8_f16_stride_tok, v8_f16_stride_head;
 
   const int32_t* cu_seqlens_q; /* int32 [batch+1] */
   const int32_t* cu_seqlens_k; /* int32 [batch+1] */
@@ -195,8 +215,8 @@ typedef struct tm_attn_tuning {
   float rescale_threshold;
   /* Kernel selection: 0 = automatic (the paired kernel when head_dim is 128,
    * block_m 128, Q is quantised in kernel, there is no bias and INT8 tiles use
-   * FP16 V; else the general kernel); 1 = always the general kernel. Other
-   * values return TM_ERR_SHAPE. */
+   * FP16 V or the fp16 copy of the V codes is given; else the general kernel);
+   * 1 = always the general kernel. Other values return TM_ERR_SHAPE. */
   int force_general;
   /* TM_NUMERICS_GPU (0) or TM_NUMERICS_EXACT (1); also the numerics of the
    * in-kernel Q quantisation. */

@@ -88,9 +88,14 @@ def test_attention_non_causal(cuda_device):
 # The INT8-V PV path (int8_use_fp16_v=False, the API's default): INT8-routed
 # tiles multiply fp16(p * sv) by the int8 V codes. block_m 64 with a random map
 # routes the two 64-row halves of a 128-row tile differently (two PVs).
+# Head_dim 128 / block_m 128 calls run on the paired kernel, whose V producer
+# loads V and / or the fp16 V codes per key tile as the item's two tiles route it.
 V8_CASES = [
     ([1024, 640], 6, 2, 128, 128, 64, "mixed"),
     ([1024], 3, 1, 128, 128, 64, "int8"),
+    ([896, 333], 3, 1, 128, 128, 64, "mixed"),       # group 3: cross-block pairs route key tiles differently
+    ([300, 700, 129], 4, 2, 128, 128, 128, "mixed"),  # varlen, mask group of 2 tiles
+    ([640, 200], 5, 5, 128, 128, 64, "mixed"),       # MHA: items of consecutive query blocks
     ([777, 64, 513], 2, 1, 64, 64, 64, "mixed"),
     ([512], 4, 4, 64, 64, 128, "mixed"),
 ]
@@ -100,6 +105,13 @@ V8_CASES = [
 @pytest.mark.parametrize("threshold", [0.0, 8.0, 15.0])
 def test_attention_int8_v_path_matches_oracle(cuda_device, lens, hq, hk, d, block_m, bnm, mode, threshold):
     mx, mean = _run_case(lens, hq, hk, d, block_m, 64, bnm, mode, threshold=threshold, fp16_v=False, seed=3)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+def test_attention_int8_v_general_kernel_matches_oracle(cuda_device, monkeypatch):
+    """The general kernel's INT8-V path (int8 V codes) at the paired kernel's shape."""
+    monkeypatch.setenv("TILEMIX_B200_KERNEL", "general")
+    mx, mean = _run_case([1024, 640], 6, 2, 128, 128, 64, 64, "mixed", fp16_v=False, seed=3)
     assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
 
 

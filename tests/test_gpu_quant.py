@@ -53,3 +53,26 @@ def test_quant_special_values(cuda_device, blk, sm_scale):
     assert np.array_equal(cus.cpu().numpy(), rcu)
     assert np.array_equal(xs.cpu().numpy().view(np.uint32), rs.view(np.uint32))
     assert np.array_equal(x8.cpu().numpy(), r8)
+
+
+@pytest.mark.parametrize("lens,h,d,blk", [([4096, 1000, 1], 8, 128, 64), ([300, 129], 3, 128, 128),
+                                          ([512], 4, 64, 64)])
+def test_quant_fp16_codes_equal_int8_codes(cuda_device, lens, h, d, blk):
+    """tm_quant_per_block_int8_f16 (the V operand of the paired kernel's INT8-V path): the
+    same scales as the int8 quantiser, and codes whose fp16 values equal the int8 codes; the
+    int8 output written alongside is unchanged."""
+    from tilemix_b200.attention.quant_per_block_varlen import per_block_int8_single
+    from tilemix_b200.attention.tilemix import _quantize_k, _quantize_v_f16
+
+    x, _, _, cu = make_qkv(lens, h, 1, d, seed=11, outliers=2)
+    x, cu = x.to(cuda_device), cu.to(cuda_device)
+    k8, ks, cuks = _quantize_k(x, cu, max(lens), blk)
+    v16, vs, cuvs = _quantize_v_f16(x, cu, max(lens), blk)
+    torch.cuda.synchronize()
+    rows = int(cuks[-1])
+    assert torch.equal(cuks, cuvs)
+    assert torch.equal(ks[:rows].view(torch.int16), vs[:rows].view(torch.int16))
+    assert v16.dtype == torch.float16
+    assert torch.equal(v16.float(), k8.float())
+    x8, _, _ = per_block_int8_single(x, cu, max(lens), BLK=blk)
+    assert torch.equal(x8, k8)

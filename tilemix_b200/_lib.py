@@ -58,6 +58,7 @@ class TmAttnParams(ctypes.Structure):
         ("k_scale", c_void_p), ("cu_k_scale", c_void_p),
         ("v8", c_void_p), ("v8_stride_tok", c_i64), ("v8_stride_head", c_i64),
         ("v_scale", c_void_p), ("cu_v_scale", c_void_p),
+        ("v8_f16", c_void_p), ("v8_f16_stride_tok", c_i64), ("v8_f16_stride_head", c_i64),
         ("cu_seqlens_q", c_void_p), ("cu_seqlens_k", c_void_p),
         ("precision_bitmask", c_void_p),
         ("bias", c_void_p), ("bias_stride", c_i64 * 4),
@@ -96,6 +97,9 @@ SIGNATURES = {
     "tm_quant_per_block_int8_ex": (c_int, [c_void_p, c_i64, c_i64, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                            c_int, ctypes.c_float, c_void_p, c_i64, c_i64, c_void_p, c_void_p,
                                            c_int, c_void_p]),
+    "tm_quant_per_block_int8_f16": (c_int, [c_void_p, c_i64, c_i64, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                            c_int, c_void_p, c_i64, c_i64, c_void_p, c_i64, c_i64, c_void_p,
+                                            c_void_p, c_int, c_void_p]),
     "tm_attn_fwd": (c_int, [ctypes.POINTER(TmAttnParams), c_void_p]),
     "tm_attn_fwd_ex": (c_int, [ctypes.POINTER(TmAttnParams), ctypes.POINTER(TmAttnTuning), c_void_p]),
     "tm_attn_fwd_noalloc": (c_int, [ctypes.POINTER(TmAttnParams), ctypes.POINTER(TmAttnTuning), c_void_p]),

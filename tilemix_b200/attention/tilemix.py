@@ -180,7 +180,8 @@ def _ptr(t: Optional[torch.Tensor]) -> ctypes.c_void_p:
 
 
 def _launch(q, k, v, o, cu_q, cu_k, bitmask, max_q, max_k, *, q8=None, sq=None, cuqs=None, k8=None, sk=None,
-            cuks=None, v8=None, sv=None, cuvs=None, bias=None, block_m, block_n, block_n_mask, BLKQ, BLKK, causal,
+            cuks=None, v8=None, sv=None, cuvs=None, v8_f16=None, bias=None, block_m, block_n, block_n_mask, BLKQ,
+            BLKK, causal,
             sm_scale, mode_code, scalar_scales, int8_use_fp16_v, threshold=None) -> None:
     p = TmAttnParams()
     p.q, p.k, p.v = _ptr(q), _ptr(k), _ptr(v)
@@ -201,6 +202,10 @@ def _launch(q, k, v, o, cu_q, cu_k, bitmask, max_q, max_k, *, q8=None, sq=None, 
     if v8 is not None:
         p.v8 = _ptr(v8)
         p.v8_stride_tok, p.v8_stride_head = v8.stride(0), v8.stride(1)
+    if v8_f16 is not None:
+        p.v8_f16 = _ptr(v8_f16)
+        p.v8_f16_stride_tok, p.v8_f16_stride_head = v8_f16.stride(0), v8_f16.stride(1)
+    if sv is not None:
         p.v_scale, p.cu_v_scale = _ptr(sv), _ptr(cuvs)
     if bias is not None:
         p.bias = _ptr(bias)
@@ -221,7 +226,7 @@ def _launch(q, k, v, o, cu_q, cu_k, bitmask, max_q, max_k, *, q8=None, sq=None, 
     p.error_flag = _ptr(_error_word(q.device))
     tune = TmAttnTuning()
     tune.rescale_threshold = rescale_threshold() if threshold is None else float(threshold)
-    tune.force_general = 1 if os.environ.get("TILEMIX_B200_KERNEL", "").strip().lower() == "general" else 0
+    tune.force_general = 1 if _force_general() else 0
     tune.numerics = numerics_code()
     stream = torch.cuda.current_stream(q.device).cuda_stream
     with torch.cuda.device(q.device):
@@ -327,6 +332,37 @@ def launch_prequantized(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q: int,
     return o, normalized_mode
 
 
+def _force_general() -> bool:
+    return os.environ.get("TILEMIX_B200_KERNEL", "").strip().lower() == "general"
+
+
+def _quantize_v_f16(v, cu_seqlens_k, max_seqlen_k, BLKK, equal_len: Optional[int] = None):
+    """V codes as exact fp16 values + fp16 block scales + int32 block offsets (the
+    quantiser of _quantize_k, writing the codes the paired kernel's INT8-V PV reads)."""
+    batch = cu_seqlens_k.numel() - 1
+    if equal_len is not None:
+        nblk = (equal_len + BLKK - 1) // BLKK
+        cu_scale_i32 = torch.arange(0, (batch + 1) * nblk, nblk, device=v.device, dtype=torch.int32)
+        n_rows = batch * nblk
+    else:
+        _, cu_scale_i32 = _scale_offsets(cu_seqlens_k, BLKK, max_seqlen_k)
+        n_rows = v.shape[0] // BLKK + batch
+    if v.stride(-1) != 1:
+        raise ValueError("the head dimension must be contiguous")
+    v16 = torch.empty(v.shape, dtype=torch.float16, device=v.device)
+    sv16 = torch.empty((n_rows, v.shape[1]), dtype=torch.float16, device=v.device)
+    cu_i32 = cu_seqlens_k.to(device=v.device, dtype=torch.int32).contiguous()
+    stream = torch.cuda.current_stream(v.device).cuda_stream
+    with torch.cuda.device(v.device):
+        rc = lib().tm_quant_per_block_int8_f16(
+            ctypes.c_void_p(v.data_ptr()), v.stride(0), v.stride(1), ctypes.c_void_p(cu_i32.data_ptr()),
+            ctypes.c_void_p(cu_scale_i32.data_ptr()), batch, v.shape[1], v.shape[2], BLKK, int(max_seqlen_k),
+            ctypes.c_void_p(0), 0, 0, ctypes.c_void_p(v16.data_ptr()), v16.stride(0), v16.stride(1),
+            ctypes.c_void_p(0), ctypes.c_void_p(sv16.data_ptr()), numerics_code(), ctypes.c_void_p(stream))
+    check(rc, "tm_quant_per_block_int8_f16")
+    return v16, sv16, cu_scale_i32
+
+
 def _quantize_k(k, cu_seqlens_k, max_seqlen_k, BLKK, equal_len: Optional[int] = None):
     """K codes + fp16 block scales + int32 block offsets, without a host sync: for varlen
     batches the scale rows are allocated for the bound sum_b ceil(T_b / BLKK) <= tokens / BLKK
@@ -378,8 +414,16 @@ def _attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q, max_s
             kw.update(q8=q8, sq=sq.to(torch.float16).contiguous(), cuqs=cuq.to(torch.int32).contiguous())
         if not int8_use_fp16_v:
             # V per BLKK block as K (tilemix.py:45-107): the INT8-V PV path of INT8-routed tiles.
-            v8, sv16, cuvs = _quantize_k(v, cu_k, max_seqlens_k, BLKK, equal_len)
-            kw.update(v8=v8, sv=sv16, cuvs=cuvs)
+            # The paired kernel (head_dim 128, block_m 128, Q quantised in kernel, no bias)
+            # reads the codes as exact fp16 values; the general kernel reads the int8 codes.
+            paired = (q.shape[-1] == 128 and block_m == 128 and BLKQ == 128 and bias is None
+                      and BLKK in (64, 128) and not _force_general())
+            if paired:
+                v16, sv16, cuvs = _quantize_v_f16(v, cu_k, max_seqlens_k, BLKK, equal_len)
+                kw.update(v8_f16=v16, sv=sv16, cuvs=cuvs)
+            else:
+                v8, sv16, cuvs = _quantize_k(v, cu_k, max_seqlens_k, BLKK, equal_len)
+                kw.update(v8=v8, sv=sv16, cuvs=cuvs)
     _launch(q, k, v, o, cu_q, cu_k, bm, max_seqlens_q, max_seqlens_k, block_m=block_m, block_n=block_n,
             block_n_mask=block_n_mask, BLKQ=BLKQ, BLKK=BLKK, causal=causal, sm_scale=sm_scale,
             mode_code=mode_code, scalar_scales=scalar_scales, int8_use_fp16_v=int8_use_fp16_v,

@@ -1,9 +1,11 @@
 // C ABI of the attention forward: argument checks, TMA descriptor encoding and
 // dispatch between the two sm_100a kernels:
 //   * paired  (attn_fwd_paired.cu): head_dim 128, block_m 128, Q quantised in
-//     kernel (or FP16-only routing) -- the model / tilemix_attention_with_quant path;
+//     kernel (or FP16-only routing), no bias; INT8-V when the fp16 copy of the
+//     V codes is given -- the model / tilemix_attention_with_quant path;
 //   * general (attn_fwd_general.cu): everything else the API accepts (block_m 64,
-//     head_dim 64, prequantised Q from launch_prequantized, bias, INT8-V).
+//     head_dim 64, prequantised Q from launch_prequantized, bias, INT8-V from
+//     the int8 codes alone).
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -17,7 +19,7 @@ int launch_attn_general(const CUtensorMap& k16, const CUtensorMap& k8, const CUt
                         const AttnArgs& a,
                         int tiles, int heads_q, int batch, cudaStream_t stream);
 int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
-                       const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
+                       const CUtensorMap& vq, const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream);
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -74,6 +76,15 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 namespace tilemix {
 
+// Whether the call's shape takes the paired kernel (INT8-V additionally needs
+// the fp16 copy of the V codes).
+static bool paired_shape(const tm_attn_params* p, const tm_attn_tuning* tuning) {
+  const bool need_int8 = p->routing_mode != TM_ROUTE_FP16;
+  const bool fuse_q = need_int8 && p->q8 == nullptr;
+  return !(tuning && tuning->force_general == 1) && p->head_dim == 128 && p->block_m == 128 && (fuse_q || !need_int8) &&
+         p->bias == nullptr;
+}
+
 // Host-side argument checks of tm_attn_fwd_ex; no CUDA call. TM_OK when the
 // call would be launched (or is an empty problem), else the status it returns.
 int check_attn_args(const tm_attn_params* p, const tm_attn_tuning* tuning) {
@@ -104,7 +115,9 @@ int check_attn_args(const tm_attn_params* p, const tm_attn_tuning* tuning) {
   }
   // INT8-V PV path: INT8-routed tiles multiply fp16(p * sv) by fp16(v8) (:449-497).
   const bool v8_path = need_int8 && !p->int8_use_fp16_v;
-  if (v8_path && (p->v8 == nullptr || p->v_scale == nullptr || p->cu_v_scale == nullptr)) return TM_ERR_NULL;
+  if (v8_path && (p->v_scale == nullptr || p->cu_v_scale == nullptr)) return TM_ERR_NULL;
+  // The int8 codes feed the general kernel, their fp16 copy the paired one.
+  if (v8_path && p->v8 == nullptr && !(p->v8_f16 != nullptr && paired_shape(p, tuning))) return TM_ERR_NULL;
   if (p->bias != nullptr && reinterpret_cast<uintptr_t>(p->bias) % 2 != 0) return TM_ERR_ALIGN;
   if (p->batch == 0 || p->max_seqlen_q == 0) return TM_OK;
   if (p->max_seqlen_k > 0 && (p->max_seqlen_k + p->block_n_mask - 1) / p->block_n_mask > 64) return TM_ERR_SHAPE;
@@ -119,7 +132,10 @@ int check_attn_args(const tm_attn_params* p, const tm_attn_tuning* tuning) {
     if (!fuse_q && (!aligned16(p->q8) || p->q8_stride_tok % 16 != 0 || p->q8_stride_head % 16 != 0))
       return TM_ERR_ALIGN;
   }
-  if (v8_path && (!aligned16(p->v8) || p->v8_stride_tok % 16 != 0 || p->v8_stride_head % 16 != 0))
+  if (v8_path && p->v8 != nullptr && (!aligned16(p->v8) || p->v8_stride_tok % 16 != 0 || p->v8_stride_head % 16 != 0))
+    return TM_ERR_ALIGN;
+  if (v8_path && p->v8_f16 != nullptr &&
+      (!aligned16(p->v8_f16) || p->v8_f16_stride_tok % 8 != 0 || p->v8_f16_stride_head % 8 != 0))
     return TM_ERR_ALIGN;
   if (p->heads_q > 65535 || p->batch > 65535) return TM_ERR_SHAPE;
   return TM_OK;
@@ -135,7 +151,6 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   if (rc0 != TM_OK) return rc0;
   if (p->batch == 0 || p->max_seqlen_q == 0) return TM_OK;
   const float rescale_threshold = tuning ? tuning->rescale_threshold : 0.f;
-  const int force_general = tuning ? tuning->force_general == 1 : 0;
   const int numerics = tuning ? tuning->numerics : TM_NUMERICS_GPU;
   const bool need_int8 = p->routing_mode != TM_ROUTE_FP16;
   const bool fuse_q = need_int8 && p->q8 == nullptr;
@@ -155,8 +170,9 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   } else {
     m_k8 = m_k16;  // never read
   }
-  CUtensorMap m_v8 = m_k8;  // read only on the INT8-V path
-  if (v8_path) {
+  CUtensorMap m_v8 = m_k8;  // read only on the INT8-V path of the general kernel
+  const bool paired = paired_shape(p, tuning) && (!v8_path || p->v8_f16 != nullptr);
+  if (v8_path && !paired) {
     rc = make_map(&m_v8, p->v8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, p->heads_k, p->k_tokens, p->v8_stride_head,
                   p->v8_stride_tok, D, D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc != TM_OK) return rc;
@@ -205,19 +221,22 @@ extern "C" int tm_attn_fwd_ex(const tm_attn_params* p, const tm_attn_tuning* tun
   a.b_sn = p->bias_stride[3];
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Bias and the INT8-V path run on the general kernel.
-  const bool paired_ok = !force_general && D == 128 && p->block_m == 128 && (fuse_q || !need_int8) && !v8_path &&
-                         p->bias == nullptr;
-  if (paired_ok) {
+  // Bias, prequantised Q and INT8-V from the int8 codes alone run on the general kernel.
+  if (paired) {
     // The paired kernel fetches all 128 dims of a tile in one 4-D copy.
-    CUtensorMap q4, k4, v4;
+    CUtensorMap q4, k4, v4, vq4;
     rc = make_map_d128(&q4, p->q, p->heads_q, p->q_tokens, p->q_stride_head, p->q_stride_tok, 128);
     if (rc != TM_OK) return rc;
     rc = make_map_d128(&k4, p->k, p->heads_k, p->k_tokens, p->k_stride_head, p->k_stride_tok, 64);
     if (rc != TM_OK) return rc;
     rc = make_map_d128(&v4, p->v, p->heads_k, p->k_tokens, p->v_stride_head, p->v_stride_tok, 64);
     if (rc != TM_OK) return rc;
-    return launch_attn_paired(q4, k4, m_k8, v4, a, p->batch, p->max_seqlen_q, st);
+    vq4 = v4;  // read only on the INT8-V path
+    if (v8_path) {
+      rc = make_map_d128(&vq4, p->v8_f16, p->heads_k, p->k_tokens, p->v8_f16_stride_head, p->v8_f16_stride_tok, 64);
+      if (rc != TM_OK) return rc;
+    }
+    return launch_attn_paired(q4, k4, m_k8, v4, vq4, a, p->batch, p->max_seqlen_q, st);
   }
   const int tiles = (p->max_seqlen_q + 127) / 128;
   return launch_attn_general(m_k16, m_k8, m_v, m_v8, a, tiles, p->heads_q, p->batch, st);

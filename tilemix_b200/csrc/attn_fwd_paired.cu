@@ -52,7 +52,7 @@ namespace paired {
 
 constexpr int kD = 128;
 constexpr int kRows = 128;
-constexpr int kStages = 3;
+constexpr int kMaxStages = 3;
 constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 
@@ -63,17 +63,26 @@ constexpr uint32_t kK8Bytes = kKeys * kD;       // 8 KB
 constexpr uint32_t kVBytes = kKeys * kD * 2;    // 16 KB
 constexpr uint32_t kOffQ16 = 0;
 constexpr uint32_t kOffQ8 = kOffQ16 + 2 * kQ16Bytes;
-constexpr uint32_t kOffK16 = kOffQ8 + 2 * kQ8Bytes;
-constexpr uint32_t kOffV = kOffK16 + kStages * kK16Bytes;
-constexpr uint32_t kOffK8 = kOffV + kStages * kVBytes;
-constexpr uint32_t kOffBar = kOffK8 + kStages * kK8Bytes;
-constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+// Shared-memory rings. FP16-V: three stages of K16, V, K8 (222.7 KB with Q).
+// INT8-V: two stages that also hold the fp16 copy of the V codes (a key tile
+// that one tile routes FP16 and the other INT8 needs both V operands).
+template <bool kV8>
+struct Smem {
+  static constexpr int kStages = kV8 ? 2 : 3;
+  static constexpr uint32_t kOffK16 = kOffQ8 + 2 * kQ8Bytes;
+  static constexpr uint32_t kOffV = kOffK16 + kStages * kK16Bytes;
+  static constexpr uint32_t kOffK8 = kOffV + kStages * kVBytes;
+  static constexpr uint32_t kOffVq = kOffK8 + kStages * kK8Bytes;
+  static constexpr uint32_t kOffBar = kOffVq + (kV8 ? kStages * kVBytes : 0u);
+  static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+};
+static_assert(Smem<false>::kSmemBytes <= 227 * 1024 && Smem<true>::kSmemBytes <= 227 * 1024, "shared memory");
 
 struct Barriers {
-  uint64_t full_k[kStages];
-  uint64_t full_v[kStages];
-  uint64_t empty_k[kStages];  // K stage free: both tiles' S of that key tile done
-  uint64_t empty_v[kStages];  // V stage free: both tiles' PV of that key tile done
+  uint64_t full_k[kMaxStages];
+  uint64_t full_v[kMaxStages];
+  uint64_t empty_k[kMaxStages];  // K stage free: both tiles' S of that key tile done
+  uint64_t empty_v[kMaxStages];  // V stage free: both tiles' PV of that key tile done
   uint64_t q_full[2];         // per item: Q tile landed (or a plain arrive when the tile is absent)
   uint64_t q_ready[2];        // per item: Q transformed by the softmax warpgroup (128 arrivals)
   uint64_t q_empty[2];        // per item: every S of the tile completed, its Q buffers may be refilled
@@ -105,6 +114,7 @@ struct Item {
   QTile tl[2];
   int q_start, seqlen_q, k_start, seqlen_k;
   int ks_base, ks_end;  // K scale-block rows of the sequence (INT8 routes)
+  int vs_base, vs_end;  // V scale-block rows of the sequence (INT8-V)
   int b, hk, n_iter;
 };
 
@@ -140,6 +150,8 @@ __device__ __forceinline__ Item load_item(int it, const AttnArgs& a, const Grid&
   m.seqlen_k = a.cu_k[z + 1] - m.k_start;
   m.ks_base = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[z] : 0;
   m.ks_end = (a.mode != TM_ROUTE_FP16) ? a.cu_ks[z + 1] : 0;
+  m.vs_base = a.v8_path ? a.cu_vs[z] : 0;
+  m.vs_end = a.v8_path ? a.cu_vs[z + 1] : 0;
   const int m_blocks = (m.seqlen_q + kRows - 1) / kRows;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
@@ -349,14 +361,19 @@ __device__ __forceinline__ void epilogue_o_row(uint32_t taddr, bool have_o, floa
   }
 }
 
-template <int kNumerics>
+// kV8: the INT8-V PV path (int8_use_fp16_v == 0): an INT8-routed tile's PV
+// is fp16(p * sv) x fp16(v8) (tilemix.py:449-497), with fp16(v8) loaded from
+// the exact fp16 copy of the V codes (tm_vq) and sv the fp16 V block scale.
+template <int kNumerics, bool kV8>
 __global__ void __launch_bounds__(kThreads, 1)
     tilemix_attn_fwd_paired_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k16,
                                    const __grid_constant__ CUtensorMap tm_k8, const __grid_constant__ CUtensorMap tm_v,
-                                   const AttnArgs a, const Grid grid) {
+                                   const __grid_constant__ CUtensorMap tm_vq, const AttnArgs a, const Grid grid) {
+  using L = Smem<kV8>;
+  constexpr int kStages = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + kOffBar);
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + L::kOffBar);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -404,6 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_v);
+      if (kV8) prefetch_tmap(&tm_vq);
     }
     bool ok = true;
     uint32_t g = 0;
@@ -462,11 +480,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             rw[x].advance();
           }
           mbar_arrive_expect_tx_e(&bars->full_k[s], (n16 ? kK16Bytes : 0u) + (n8 ? kK8Bytes : 0u));
-          if (n16) tma_load_4d_e(smem + kOffK16 + s * kK16Bytes, &tm_k16, &bars->full_k[s], 0, tok, 0, m.hk);
-          if (n8) tma_load_3d_e(smem + kOffK8 + s * kK8Bytes, &tm_k8, &bars->full_k[s], 0, m.hk, tok);
+          if (n16) tma_load_4d_e(smem + L::kOffK16 + s * kK16Bytes, &tm_k16, &bars->full_k[s], 0, tok, 0, m.hk);
+          if (n8) tma_load_3d_e(smem + L::kOffK8 + s * kK8Bytes, &tm_k8, &bars->full_k[s], 0, m.hk, tok);
         } else {
-          mbar_arrive_expect_tx_e(&bars->full_v[s], kVBytes);
-          tma_load_4d_e(smem + kOffV + s * kVBytes, &tm_v, &bars->full_v[s], 0, tok, 0, m.hk);
+          // FP16-V: V for every key tile. INT8-V: V for the tiles that route the
+          // key tile FP16, the fp16 V codes for those that route it INT8.
+          bool v16 = true, vq = false;
+          if (kV8) {
+            v16 = false;
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+              if (j < tile_of(m, x).nb) {
+                if (rw[x].kind())
+                  vq = true;
+                else
+                  v16 = true;
+              }
+              rw[x].advance();
+            }
+          }
+          mbar_arrive_expect_tx_e(&bars->full_v[s], (v16 ? kVBytes : 0u) + (vq ? kVBytes : 0u));
+          if (v16) tma_load_4d_e(smem + L::kOffV + s * kVBytes, &tm_v, &bars->full_v[s], 0, tok, 0, m.hk);
+          if (kV8 && vq) tma_load_4d_e(smem + L::kOffVq + s * kVBytes, &tm_vq, &bars->full_v[s], 0, tok, 0, m.hk);
         }
       }
       ++n;
@@ -499,9 +534,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t idesc_pv = make_idesc(1, 0, 0, 1, 128, kD);
     const uint64_t dq16 = make_sdesc(smem_u32(smem + kOffQ16 + x * kQ16Bytes), 16, 1024, 2);
     const uint64_t dq8 = make_sdesc(smem_u32(smem + kOffQ8 + x * kQ8Bytes), 16, 1024, 2);
-    const uint64_t dk16 = make_sdesc(smem_u32(smem + kOffK16), 16, 1024, 2);
-    const uint64_t dk8 = make_sdesc(smem_u32(smem + kOffK8), 16, 1024, 2);
-    const uint64_t dv = make_sdesc(smem_u32(smem + kOffV), kVBytes / 2, 1024, 2);
+    const uint64_t dk16 = make_sdesc(smem_u32(smem + L::kOffK16), 16, 1024, 2);
+    const uint64_t dk8 = make_sdesc(smem_u32(smem + L::kOffK8), 16, 1024, 2);
+    const uint64_t dv = make_sdesc(smem_u32(smem + L::kOffV), kVBytes / 2, 1024, 2);
+    const uint64_t dvq = make_sdesc(smem_u32(smem + L::kOffVq), kVBytes / 2, 1024, 2);
     const uint32_t d_o = tbase + col_o(x);
     bool ok = true;
     uint32_t g = 0;   // key tiles over all items
@@ -518,8 +554,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->q_ready[x], n & 1, a.err, kErrTimeoutQ));
       tc_fence_after();
       if (nb == 0) tc_commit_e(&bars->q_empty[x]);
-      RouteWalker rw;
+      RouteWalker rw, rw_pv;
       rw.init(a.mode, tile_of(m, x).bits, a.block_n_mask);
+      rw_pv.init(a.mode, tile_of(m, x).bits, a.block_n_mask);
       for (int j = 0; j <= m.n_iter && ok; ++j) {
         if (j < m.n_iter) {
           const uint32_t gj = g + j;
@@ -561,6 +598,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int jj = j - 1;
           const uint32_t gj = g + jj;
           const uint32_t st = gj % kStages;
+          const int kind_pv = rw_pv.kind();  // route of key tile jj (INT8-V operand choice)
+          rw_pv.advance();
           ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->full_v[st], (gj / kStages) & 1, a.err, kErrTimeoutFull));
           if (!ok) break;
           if (jj < nb) {
@@ -572,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->o_free[x], (n - 1) & 1, a.err, kErrTimeoutOFree));
             if (!ok) break;
             tc_fence_after();
-            const uint64_t vb = dv + ((st * kVBytes) >> 4);
+            const uint64_t vb = (kV8 && kind_pv == 1 ? dvq : dv) + ((st * kVBytes) >> 4);
             const uint32_t pa = tbase + col_s(x, c & 1);
 #pragma unroll
             for (int kk = 0; kk < kKeys / 16; ++kk)
@@ -643,6 +682,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         return v;
       };
       __half sk_next = load_next_sk();
+      // INT8-V: V block scale of a tile, tracked and loaded like the K scale
+      // (1 when the sequence has no scale rows, the reference's masked load).
+      const int vs_end = m.vs_end;
+      const bool have_sv = kV8 && vs_end > m.vs_base;
+      const __half* sv_col = a.v_scale + m.hk;
+      int sv_idx = m.vs_base, sv_sub = 0;
+      auto load_next_sv = [&]() -> __half {
+        const __half v = have_sv ? sv_col[static_cast<int64_t>(min(sv_idx, vs_end - 1)) * a.HK] : __half();
+        if (++sv_sub == sk_per) {
+          sv_sub = 0;
+          ++sv_idx;
+        }
+        return v;
+      };
+      __half sv_next = kV8 ? load_next_sv() : __half();
       for (int j = 0; ok && j < nb; ++j) {
         const uint32_t c = cx + j;
         const int slot = c & 1;
@@ -650,6 +704,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         rw.advance();
         const __half sk16 = (have_sk && kind == 1) ? sk_next : __float2half_rn(1.f);
         sk_next = load_next_sk();
+        __half sv16 = __float2half_rn(1.f);
+        if (kV8) {
+          if (have_sv && kind == 1) sv16 = sv_next;
+          sv_next = load_next_sv();
+        }
         const float ss = kind == 1 ? int8_score_scale(sq16, sk16, a.qk_scale) : 1.f;
         ok = __all_sync(0xffffffffu, mbar_wait_spin(&bars->s_full[x][slot], (c >> 1) & 1, a.err, kErrTimeoutScores));
         if (!ok) break;
@@ -660,6 +719,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool need_rescale;
         softmax_tile<kNumerics>(tbase + lane_off + col_s(x, slot), kind, ss, lim, a.rescale_threshold, m_used, l, p, o_scale,
                      need_rescale);
+        if (kV8 && kind == 1) {
+          // p_scaled = fp16(p * sv): the product of two fp16 values rounded once
+          // (l above summed the unscaled p, as the reference's l_tile does).
+          const __half2 sv2 = __halves2half2(sv16, sv16);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&p[i]), sv2);
+            p[i] = *reinterpret_cast<const uint32_t*>(&r);
+          }
+        }
         // P goes out first; its store overlaps the wait for the previous PV
         // when O has to be rescaled (PV(c-1) must have accumulated into O).
         tmem_st32(tbase + lane_off + col_s(x, slot), p);
@@ -717,17 +786,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace paired
 
 int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUtensorMap& k8, const CUtensorMap& v,
-                       const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream) {
+                       const CUtensorMap& vq, const AttnArgs& a, int batch, int max_seqlen_q, cudaStream_t stream) {
   using namespace paired;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TM_ERR_LAUNCH;
   static bool attr_set[64] = {};
   static int n_sm[64] = {};
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel<kNumericsGpu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
-        cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel<kNumericsExact>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) != cudaSuccess)
+    const int b16 = static_cast<int>(Smem<false>::kSmemBytes), b8 = static_cast<int>(Smem<true>::kSmemBytes);
+    if (cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel<kNumericsGpu, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, b16) != cudaSuccess ||
+        cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel<kNumericsExact, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, b16) != cudaSuccess ||
+        cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel<kNumericsGpu, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, b8) != cudaSuccess ||
+        cudaFuncSetAttribute(tilemix_attn_fwd_paired_kernel<kNumericsExact, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, b8) != cudaSuccess)
       return TM_ERR_LAUNCH;
     if (cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm[dev] <= 0)
       return TM_ERR_LAUNCH;
@@ -746,10 +820,17 @@ int launch_attn_paired(const CUtensorMap& q, const CUtensorMap& k16, const CUten
   const int ctas = static_cast<int>(std::min<int64_t>(items, n_sm[dev]));
   // Long units (at least two grids' worth of levels): one unit's levels per round.
   g.chunk = g.nx >= 2 * ctas ? ctas : 1;
-  if (a.numerics == kNumericsGpu)
-    tilemix_attn_fwd_paired_kernel<kNumericsGpu><<<ctas, kThreads, kSmemBytes, stream>>>(q, k16, k8, v, a, g);
-  else
-    tilemix_attn_fwd_paired_kernel<kNumericsExact><<<ctas, kThreads, kSmemBytes, stream>>>(q, k16, k8, v, a, g);
+  const uint32_t b16 = Smem<false>::kSmemBytes, b8 = Smem<true>::kSmemBytes;
+  if (a.v8_path) {
+    if (a.numerics == kNumericsGpu)
+      tilemix_attn_fwd_paired_kernel<kNumericsGpu, true><<<ctas, kThreads, b8, stream>>>(q, k16, k8, v, vq, a, g);
+    else
+      tilemix_attn_fwd_paired_kernel<kNumericsExact, true><<<ctas, kThreads, b8, stream>>>(q, k16, k8, v, vq, a, g);
+  } else if (a.numerics == kNumericsGpu) {
+    tilemix_attn_fwd_paired_kernel<kNumericsGpu, false><<<ctas, kThreads, b16, stream>>>(q, k16, k8, v, vq, a, g);
+  } else {
+    tilemix_attn_fwd_paired_kernel<kNumericsExact, false><<<ctas, kThreads, b16, stream>>>(q, k16, k8, v, vq, a, g);
+  }
   return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_LAUNCH;
 }
 

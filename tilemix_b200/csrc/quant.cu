@@ -137,7 +137,8 @@ template <int kNumerics, int DIM, int BLK>
 __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_unit_kernel(
     const __half* __restrict__ x, int64_t x_stride_tok, int64_t x_stride_head, const int32_t* __restrict__ cu_seqlens,
     const int32_t* __restrict__ cu_scale, int heads, int8_t* __restrict__ out, int64_t o_stride_tok,
-    int64_t o_stride_head, float* __restrict__ scale_f32, __half* __restrict__ scale_f16) {
+    int64_t o_stride_head, float* __restrict__ scale_f32, __half* __restrict__ scale_f16,
+    __half* __restrict__ out16 = nullptr, int64_t o16_stride_tok = 0, int64_t o16_stride_head = 0) {
   constexpr int kVecPerRow = DIM / 8;
   constexpr int kVecs = BLK * kVecPerRow / kQuantThreads;  // 16-byte vectors per thread
   __shared__ float red[kQuantThreads / 32];
@@ -148,7 +149,9 @@ __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_unit_kerne
   const int rows = min(BLK, len - off_blk * BLK);
   const int64_t tok0 = static_cast<int64_t>(start) + static_cast<int64_t>(off_blk) * BLK;
   const __half* xb = x + tok0 * x_stride_tok + static_cast<int64_t>(off_h) * x_stride_head;
-  int8_t* ob = out + tok0 * o_stride_tok + static_cast<int64_t>(off_h) * o_stride_head;
+  int8_t* ob = out == nullptr ? nullptr : out + tok0 * o_stride_tok + static_cast<int64_t>(off_h) * o_stride_head;
+  __half* ob16 =
+      out16 == nullptr ? nullptr : out16 + tok0 * o16_stride_tok + static_cast<int64_t>(off_h) * o16_stride_head;
   const int c = (threadIdx.x % kVecPerRow) * 8;
   uint4 v[kVecs];
   uint32_t am2 = 0u;
@@ -188,7 +191,18 @@ __global__ void __launch_bounds__(kQuantThreads) quant_per_block_int8_unit_kerne
     }
     const uint32_t lo = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410);
     const uint32_t hi = __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410);
-    *reinterpret_cast<uint2*>(ob + r * o_stride_tok + c) = make_uint2(lo, hi);
+    if (ob != nullptr) *reinterpret_cast<uint2*>(ob + r * o_stride_tok + c) = make_uint2(lo, hi);
+    if (ob16 != nullptr) {
+      // The same codes as exact fp16 values (small integers).
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __half2 h2 = __halves2half2(__short2half_rn(static_cast<short>(static_cast<int8_t>(u[2 * e] & 0xFFu))),
+                                          __short2half_rn(static_cast<short>(static_cast<int8_t>(u[2 * e + 1] & 0xFFu))));
+        w[e] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      *reinterpret_cast<uint4*>(ob16 + r * o16_stride_tok + c) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
   }
   if (threadIdx.x == 0) {
     const int64_t sidx = (static_cast<int64_t>(cu_scale[off_b]) + off_blk) * heads + off_h;
@@ -205,23 +219,27 @@ template <int kNumerics>
 int launch_quant(const void* x, int64_t x_stride_tok, int64_t x_stride_head, const int32_t* cu_seqlens,
                  const int32_t* cu_scale, int heads, int dim, int blk, float sm_scale, int8_t* out,
                  int64_t out_stride_tok, int64_t out_stride_head, float* scale_f32, void* scale_f16, dim3 grid,
-                 cudaStream_t st) {
+                 cudaStream_t st, void* out16 = nullptr, int64_t o16_st = 0, int64_t o16_sh = 0) {
   using namespace tilemix;
   const __half* xh = static_cast<const __half*>(x);
   __half* s16 = static_cast<__half*>(scale_f16);
   if (sm_scale == 1.0f && (dim == 64 || dim == 128) && (blk == 64 || blk == 128)) {
     if (dim == 128 && blk == 64)
       quant_per_block_int8_unit_kernel<kNumerics, 128, 64><<<grid, kQuantThreads, 0, st>>>(
-          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16,
+          static_cast<__half*>(out16), o16_st, o16_sh);
     else if (dim == 128)
       quant_per_block_int8_unit_kernel<kNumerics, 128, 128><<<grid, kQuantThreads, 0, st>>>(
-          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16,
+          static_cast<__half*>(out16), o16_st, o16_sh);
     else if (blk == 64)
       quant_per_block_int8_unit_kernel<kNumerics, 64, 64><<<grid, kQuantThreads, 0, st>>>(
-          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16,
+          static_cast<__half*>(out16), o16_st, o16_sh);
     else
       quant_per_block_int8_unit_kernel<kNumerics, 64, 128><<<grid, kQuantThreads, 0, st>>>(
-          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16);
+          xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, out, out_stride_tok, out_stride_head, scale_f32, s16,
+          static_cast<__half*>(out16), o16_st, o16_sh);
   } else {
     quant_per_block_int8_kernel<kNumerics><<<grid, kQuantThreads, 0, st>>>(
         xh, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, dim, blk, sm_scale, out, out_stride_tok,
@@ -257,6 +275,37 @@ extern "C" int tm_quant_per_block_int8_ex(const void* x, int64_t x_stride_tok, i
   return launch_quant<tilemix::kNumericsExact>(x, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, dim, blk,
                                                 sm_scale, out, out_stride_tok, out_stride_head, scale_f32, scale_f16,
                                                 grid, st);
+}
+
+extern "C" int tm_quant_per_block_int8_f16(const void* x, int64_t x_stride_tok, int64_t x_stride_head,
+                                           const int32_t* cu_seqlens, const int32_t* cu_scale, int batch, int heads,
+                                           int dim, int blk, int max_seqlen, int8_t* out, int64_t out_stride_tok,
+                                           int64_t out_stride_head, void* out_f16, int64_t out_f16_stride_tok,
+                                           int64_t out_f16_stride_head, float* scale_f32, void* scale_f16,
+                                           int numerics, void* stream) {
+  if (x == nullptr || out_f16 == nullptr || cu_seqlens == nullptr || cu_scale == nullptr) return TM_ERR_NULL;
+  if (batch < 0 || heads <= 0 || max_seqlen < 0) return TM_ERR_SHAPE;
+  if (numerics != TM_NUMERICS_GPU && numerics != TM_NUMERICS_EXACT) return TM_ERR_SHAPE;
+  if ((dim != 64 && dim != 128) || (blk != 64 && blk != 128)) return TM_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0 || (x_stride_tok & 7) != 0 || (x_stride_head & 7) != 0)
+    return TM_ERR_ALIGN;
+  if (out != nullptr &&
+      ((reinterpret_cast<uintptr_t>(out) & 7u) != 0 || (out_stride_tok & 7) != 0 || (out_stride_head & 7) != 0))
+    return TM_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(out_f16) & 15u) != 0 || (out_f16_stride_tok & 7) != 0 ||
+      (out_f16_stride_head & 7) != 0)
+    return TM_ERR_ALIGN;
+  if (heads > 65535 || batch > 65535) return TM_ERR_SHAPE;
+  if (batch == 0 || max_seqlen == 0) return TM_OK;
+  dim3 grid((max_seqlen + blk - 1) / blk, heads, batch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (numerics == TM_NUMERICS_GPU)
+    return launch_quant<tilemix::kNumericsGpu>(x, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, dim, blk,
+                                                1.0f, out, out_stride_tok, out_stride_head, scale_f32, scale_f16, grid,
+                                                st, out_f16, out_f16_stride_tok, out_f16_stride_head);
+  return launch_quant<tilemix::kNumericsExact>(x, x_stride_tok, x_stride_head, cu_seqlens, cu_scale, heads, dim, blk,
+                                                1.0f, out, out_stride_tok, out_stride_head, scale_f32, scale_f16, grid,
+                                                st, out_f16, out_f16_stride_tok, out_f16_stride_head);
 }
 
 extern "C" int tm_quant_per_block_int8(const void* x, int64_t x_stride_tok, int64_t x_stride_head,
