@@ -114,16 +114,17 @@ __device__ __forceinline__ void softmax_tile(uint32_t taddr, int kind, float ss,
                                              float& m_used, float& l, uint32_t (&p)[32], float& o_scale,
                                              bool& need_rescale, const __half* brow = nullptr,
                                              int64_t bstride = 0) {
-  uint32_t s[64];
-  tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-  tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-  tmem_wait_ld();
   // qk of the row as fp16 pairs: h[i] = (qk[2i], qk[2i+1]).
   uint32_t h[32];
   if (kNumerics == kNumericsGpu && kind == 0) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) h[i] = __byte_perm(s[2 * i], s[2 * i + 1], 0x5410);
+    // fp16 accumulator: the load packs the columns' 16-bit values in pairs.
+    tmem_ld64_pack16(taddr, h);
+    tmem_wait_ld();
   } else {
+    uint32_t s[64];
+    tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+    tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+    tmem_wait_ld();
     if (kind != 0) {
       // f32(i) * ss in one rounding: with a = float(i + 0x4B400000) = 1.5*2^23 + i,
       // fma(a, ss, -1.5*2^23*ss) evaluates a*ss - 1.5*2^23*ss = i*ss exactly before

@@ -30,8 +30,10 @@
 //                     (fp16(q * sm_scale * log2e)) and quantise it per 128-row
 //                     block into the INT8 operand (BLKQ = 128 block = the tile).
 //   warp 8            TMA producer of K (only the formats routed by either tile),
-//                     64 keys per stage of a 3-stage ring
-//   warp 10           TMA producer of the Q tiles, then of V (same ring stages)
+//                     64 keys per stage of a 3-stage ring (2 stages on the INT8-V
+//                     path, whose stages also hold the fp16 V codes)
+//   warp 10           TMA producer of the Q tiles, then of V (same ring stages;
+//                     on the INT8-V path V and / or the fp16 V codes, as routed)
 //                     Every K16 / V / Q tile arrives in a single 4-D copy (all 128
 //                     dims), so each producer issues at most two copies per stage:
 //                     a thread's bulk-tensor copies go out one after another, and
@@ -231,12 +233,14 @@ __device__ __forceinline__ __half transform_q(uint8_t* smem, Barriers* bars, con
     return reinterpret_cast<uint4*>(q16 + (c >> 3) * (kQ16Bytes / 2) + t * 128 + (((c & 7) ^ (t & 7)) << 4));
   };
   const uint64_t qk2 = f32x2_pack(a.qk_scale, a.qk_scale);
-  auto scale_pair = [&](uint32_t h2) {  // fp16(x * qk_scale) of a pair
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+  auto scale_f2 = [&](float2 f) {  // fp16(x * qk_scale) of a pair already in fp32
     uint64_t r;
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f32x2_pack(f.x, f.y)), "l"(qk2));
     const float2 v = f32x2_unpack(r);
     return pack_half2_rn(v.x, v.y);
+  };
+  auto scale_pair = [&](uint32_t h2) {  // fp16(x * qk_scale) of a pair
+    return scale_f2(__half22float2(*reinterpret_cast<const __half2*>(&h2)));
   };
   if (a.mode == TM_ROUTE_FP16) {
 #pragma unroll 4
@@ -279,10 +283,12 @@ __device__ __forceinline__ __half transform_q(uint8_t* smem, Barriers* bars, con
     // 16 codes of dims [16g, 16g+16) = chunks 2g and 2g+1
     const uint4 ra = *chunk(2 * g), rb = *chunk(2 * g + 1);
     const uint32_t hw[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
-    uint32_t u[16];
+    uint32_t u[16], sc[8];
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
+      // One conversion of the pair serves the codes and the scaled fp16 copy.
       const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hw[p]));
+      sc[p] = scale_f2(f);
       if (finite) {
         quant_code_pair<kNumerics>(f.x, f.y, qd, &u[2 * p], &u[2 * p + 1]);
       } else {
@@ -296,8 +302,8 @@ __device__ __forceinline__ __half transform_q(uint8_t* smem, Barriers* bars, con
       w[i] = __byte_perm(__byte_perm(u[4 * i], u[4 * i + 1], 0x0040), __byte_perm(u[4 * i + 2], u[4 * i + 3], 0x0040),
                          0x5410);
     *reinterpret_cast<uint4*>(q8 + t * 128 + ((g ^ (t & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-    *chunk(2 * g) = make_uint4(scale_pair(hw[0]), scale_pair(hw[1]), scale_pair(hw[2]), scale_pair(hw[3]));
-    *chunk(2 * g + 1) = make_uint4(scale_pair(hw[4]), scale_pair(hw[5]), scale_pair(hw[6]), scale_pair(hw[7]));
+    *chunk(2 * g) = make_uint4(sc[0], sc[1], sc[2], sc[3]);
+    *chunk(2 * g + 1) = make_uint4(sc[4], sc[5], sc[6], sc[7]);
   }
   fence_proxy_async_smem();
   return __float2half_rn(scale);
