@@ -652,8 +652,9 @@ def run_ours(args) -> None:
     cpu_line = None
     if want_cpu:
         try:
+            # Four whole (sequence, Q head) units per core: ~13 s of CPU work on the B200 host.
             tasks, cflops, sample = cpu_units(q_cpu.numpy(), k_cpu.numpy(), v_cpu.numpy(), oracle_map_words(),
-                                              cpu_cores, 8.0)
+                                              4 * cpu_cores, 8.0)
             t0 = time.perf_counter()
             pool.map(run_unit_proxy(), tasks, chunksize=1)
             dt = time.perf_counter() - t0

@@ -122,3 +122,45 @@ def test_attention_requires_cuda_tensors():
     with pytest.raises(RuntimeError):
         tilemix_attention_with_quant(q, q, q, cu, cu, 128, 128, pm, block_m=128, block_n=64, causal=True,
                                      routing_mode="mixed")
+
+
+class _FakeTensor:
+    """Just the attributes the argument checks read (no device needed)."""
+
+    def __init__(self, shape, dtype=torch.float16, device="cuda:0", is_cuda=True):
+        self.shape, self.dtype, self.device, self.is_cuda = torch.Size(shape), dtype, torch.device(device), is_cuda
+        self.ndim = len(shape)
+
+    def numel(self):
+        n = 1
+        for s in self.shape:
+            n *= s
+        return n
+
+
+@pytest.mark.parametrize("change,exc,text", [
+    (dict(q=_FakeTensor((64, 4, 64), is_cuda=False)), RuntimeError, "CUDA-only"),
+    (dict(q=_FakeTensor((64, 4, 64, 1))), ValueError, "flattened"),
+    (dict(v=_FakeTensor((64, 1, 64))), ValueError, "K/V shapes"),
+    (dict(q=_FakeTensor((64, 3, 64))), ValueError, "divisible"),
+    (dict(v=_FakeTensor((64, 2, 64), device="cuda:1")), ValueError, "one CUDA device"),
+    (dict(v=_FakeTensor((64, 2, 64), dtype=torch.bfloat16)), TypeError, "one dtype"),
+    (dict(max_k=32), ValueError, "equal Q/K lengths"),
+    (dict(block_n_mask=96), ValueError, "multiple of block_n"),
+    (dict(max_q=64 * 65, max_k=64 * 65), ValueError, "64 mask blocks"),
+    (dict(BLKQ=128), ValueError, "scalar_scales"),
+    (dict(bitmask=_FakeTensor((2,), dtype=torch.int64)), TypeError, "torch.uint64"),
+    (dict(bitmask=_FakeTensor((3,), dtype=torch.uint64)), ValueError, "rows, expected 2"),
+])
+def test_validate_order_and_messages(change, exc, text):
+    """launch_prequantized's checks (tilemix.py:1167-1201): the first failing rule raises the
+    reference's exception type and message; a valid call raises nothing."""
+    from tilemix_b200.attention.tilemix import _validate
+
+    args = dict(q=_FakeTensor((64, 4, 64)), k=_FakeTensor((64, 2, 64)), v=_FakeTensor((64, 2, 64)), max_q=64,
+                max_k=64, bitmask=_FakeTensor((2,), dtype=torch.uint64), block_m=64, block_n=64, block_n_mask=64,
+                BLKQ=64, BLKK=64, scalar_scales=True)
+    _validate(**args)
+    args.update(change)
+    with pytest.raises(exc, match=text):
+        _validate(**args)
