@@ -264,33 +264,12 @@ def launch_prequantized(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q: int,
                         routing_mode: RoutingMode = "auto", run_length: bool = False, scalar_scales: bool = True,
                         int8_cache_ca: bool = False, int8_use_fp16_v: bool = False):
     """Launch the attention kernel on prequantised Q/K(/V) (tilemix.py:1132-1336)."""
-    if not q.is_cuda:
-        raise RuntimeError("TileMix is a CUDA-only kernel")
-    if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
-        raise ValueError("expected flattened [tokens, heads, dim] tensors")
-    if k.shape != v.shape or q.shape[-1] != k.shape[-1]:
-        raise ValueError("K/V shapes and Q/K/V head dimensions must match")
-    if q.shape[1] % k.shape[1] != 0:
-        raise ValueError("Q heads must be divisible by KV heads")
-    if q.device != k.device or q.device != v.device:
-        raise ValueError("q, k, and v must share one CUDA device")
-    if q.dtype != k.dtype or q.dtype != v.dtype:
-        raise TypeError("q, k, and v must share one dtype")
-    if max_seqlens_q != max_seqlens_k:
-        raise ValueError("packed routing currently requires equal Q/K lengths")
     if block_n_mask is None:
         block_n_mask = block_n
-    if block_n_mask % block_n:
-        raise ValueError("block_n_mask must be a multiple of block_n")
-    if (max_seqlens_k + block_n_mask - 1) // block_n_mask > 64:
-        raise ValueError("packed routing exceeds 64 mask blocks")
-    if scalar_scales and (block_m != BLKQ or block_n != BLKK):
-        raise ValueError("scalar_scales requires block_m == BLKQ and block_n == BLKK")
-    expected_rows = k.shape[1] * ((max_seqlens_q + block_m - 1) // block_m)
-    if precision_bitmask.dtype != torch.uint64:
-        raise TypeError("precision_bitmask must be torch.uint64")
-    if precision_bitmask.numel() != expected_rows:
-        raise ValueError(f"precision_bitmask has {precision_bitmask.numel()} rows, expected {expected_rows}")
+    # The reference's order: layout checks, routing classification, quantised tensors, then
+    # the head-dimension limit.
+    _validate(q, k, v, max_seqlens_q, max_seqlens_k, precision_bitmask, block_m, block_n, block_n_mask, BLKQ,
+              BLKK, scalar_scales, head_dim_rule=False)
     normalized_mode = routing_mode.strip().lower()
     if normalized_mode == "auto":
         normalized_mode = classify_bitmask_routing(precision_bitmask, seqlen_q=max_seqlens_q,
@@ -298,12 +277,13 @@ def launch_prequantized(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q: int,
                                                    block_n_mask=block_n_mask, causal=causal)
     mode_code = _routing_mode_code(normalized_mode)
     quant_tensors = (q8, k8, v8, sQ_blocks, sK_blocks, sV_blocks, cu_q_scale, cu_k_scale, cu_v_scale)
-    if any(t.device != q.device for t in quant_tensors):
-        raise ValueError("all quantization tensors must share q.device")
-    if q8.dtype != torch.int8 or k8.dtype != torch.int8:
-        raise TypeError("q8 and k8 must be torch.int8")
-    if v8.dtype != torch.int8:
-        raise TypeError("v8 must be torch.int8")
+    _raise_first((
+        (lambda: any(t.device != q.device for t in quant_tensors),
+         ValueError("all quantization tensors must share q.device")),
+        (lambda: {q8.dtype, k8.dtype} != {torch.int8}, TypeError("q8 and k8 must be torch.int8")),
+        (lambda: v8.dtype != torch.int8, TypeError("v8 must be torch.int8")),
+        (lambda: q.shape[-1] > 128, ValueError("head dimension must be <= 128")),
+    ))
     if sm_scale is None:
         sm_scale = q.shape[-1] ** -0.5
     if o is None:
@@ -311,11 +291,6 @@ def launch_prequantized(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q: int,
     cu_seqlens_q = cu_seqlens_q.to(device=q.device, dtype=torch.int32).contiguous()
     cu_seqlens_k = cu_seqlens_k.to(device=q.device, dtype=torch.int32).contiguous()
     precision_bitmask = precision_bitmask.to(device=q.device, dtype=torch.uint64).contiguous()
-    head_dim = q.shape[-1]
-    padded_head_dim = max(32, 1 << (head_dim - 1).bit_length())
-    padded_head_dim = ((padded_head_dim + 31) // 32) * 32
-    if padded_head_dim > 128:
-        raise ValueError("head dimension must be <= 128")
     int8_path = mode_code != ROUTING_MODE_FP16
     _check_kernel_support(q, block_m, block_n, BLKK, int8_path, int8_use_fp16_v, bias, max_seqlens_q, max_seqlens_k)
     kw = {}
@@ -457,13 +432,22 @@ def tilemix_attention_with_quant(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen
     return o, normalized_mode
 
 
-def _validate(q, k, v, max_q, max_k, bitmask, block_m, block_n, block_n_mask, BLKQ, BLKK, scalar_scales):
+def _raise_first(rules) -> None:
+    """Raise the exception of the first rule whose predicate holds (rules in order)."""
+    for failing, error in rules:
+        if failing():
+            raise error
+
+
+def _validate(q, k, v, max_q, max_k, bitmask, block_m, block_n, block_n_mask, BLKQ, BLKK, scalar_scales,
+              head_dim_rule: bool = True):
     """Argument checks of launch_prequantized (tilemix.py:1167-1201): the same exception types
     and messages, in the same order, so callers see the reference's first error. Each rule is
     a (predicate of a failing call, exception) pair evaluated lazily; later rules may assume
-    the earlier ones held."""
+    the earlier ones held. ``head_dim_rule=False`` leaves the head-dimension limit to the
+    caller (launch_prequantized checks it after its quantised tensors, as the reference)."""
     rows = k.shape[1] * ((max_q + block_m - 1) // block_m) if k.ndim == 3 else 0
-    rules = (
+    _raise_first((
         (lambda: not q.is_cuda, RuntimeError("TileMix is a CUDA-only kernel")),
         (lambda: 3 != q.ndim or 3 != k.ndim or 3 != v.ndim,
          ValueError("expected flattened [tokens, heads, dim] tensors")),
@@ -480,178 +464,7 @@ def _validate(q, k, v, max_q, max_k, bitmask, block_m, block_n, block_n_mask, BL
         (lambda: bitmask.dtype != torch.uint64, TypeError("precision_bitmask must be torch.uint64")),
         (lambda: bitmask.numel() != rows,
          ValueError(f"precision_bitmask has {bitmask.numel()} rows, expected {rows}")),
-        (lambda: q.shape[-1] > 128, ValueError("head dimension must be <= 128")),
-    )
-    for failing, error in rules:
-        if failing():
-            raise error
-    int8_path = mode_code != ROUTING_MODE_FP16
-    _check_kernel_support(q, block_m, block_n, BLKK, int8_path, int8_use_fp16_v, bias, max_seqlens_q, max_seqlens_k)
-    kw = {}
-    if int8_path:
-        kw = dict(q8=q8, sq=sQ_blocks.to(torch.float16).contiguous(), cuqs=cu_q_scale.to(torch.int32).contiguous(),
-                  k8=k8, sk=sK_blocks.to(torch.float16).contiguous(), cuks=cu_k_scale.to(torch.int32).contiguous())
-        if not int8_use_fp16_v:
-            kw.update(v8=v8, sv=sV_blocks.to(torch.float16).contiguous(),
-                      cuvs=cu_v_scale.to(torch.int32).contiguous())
-    _launch(q, k, v, o, cu_seqlens_q, cu_seqlens_k, precision_bitmask, max_seqlens_q, max_seqlens_k,
-            block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, BLKQ=BLKQ, BLKK=BLKK, causal=causal,
-            sm_scale=sm_scale, mode_code=mode_code, scalar_scales=scalar_scales,
-            int8_use_fp16_v=int8_use_fp16_v, bias=bias, **kw)
-    return o, normalized_mode
+        (lambda: head_dim_rule and q.shape[-1] > 128, ValueError("head dimension must be <= 128")),
+    ))
 
 
-def _force_general() -> bool:
-    return os.environ.get("TILEMIX_B200_KERNEL", "").strip().lower() == "general"
-
-
-def _quantize_v_f16(v, cu_seqlens_k, max_seqlen_k, BLKK, equal_len: Optional[int] = None):
-    """V codes as exact fp16 values + fp16 block scales + int32 block offsets (the
-    quantiser of _quantize_k, writing the codes the paired kernel's INT8-V PV reads)."""
-    batch = cu_seqlens_k.numel() - 1
-    if equal_len is not None:
-        nblk = (equal_len + BLKK - 1) // BLKK
-        cu_scale_i32 = torch.arange(0, (batch + 1) * nblk, nblk, device=v.device, dtype=torch.int32)
-        n_rows = batch * nblk
-    else:
-        _, cu_scale_i32 = _scale_offsets(cu_seqlens_k, BLKK, max_seqlen_k)
-        n_rows = v.shape[0] // BLKK + batch
-    if v.stride(-1) != 1:
-        raise ValueError("the head dimension must be contiguous")
-    v16 = torch.empty(v.shape, dtype=torch.float16, device=v.device)
-    sv16 = torch.empty((n_rows, v.shape[1]), dtype=torch.float16, device=v.device)
-    cu_i32 = cu_seqlens_k.to(device=v.device, dtype=torch.int32).contiguous()
-    stream = torch.cuda.current_stream(v.device).cuda_stream
-    with torch.cuda.device(v.device):
-        rc = lib().tm_quant_per_block_int8_f16(
-            ctypes.c_void_p(v.data_ptr()), v.stride(0), v.stride(1), ctypes.c_void_p(cu_i32.data_ptr()),
-            ctypes.c_void_p(cu_scale_i32.data_ptr()), batch, v.shape[1], v.shape[2], BLKK, int(max_seqlen_k),
-            ctypes.c_void_p(0), 0, 0, ctypes.c_void_p(v16.data_ptr()), v16.stride(0), v16.stride(1),
-            ctypes.c_void_p(0), ctypes.c_void_p(sv16.data_ptr()), numerics_code(), ctypes.c_void_p(stream))
-    check(rc, "tm_quant_per_block_int8_f16")
-    return v16, sv16, cu_scale_i32
-
-
-def _quantize_k(k, cu_seqlens_k, max_seqlen_k, BLKK, equal_len: Optional[int] = None):
-    """K codes + fp16 block scales + int32 block offsets, without a host sync: for varlen
-    batches the scale rows are allocated for the bound sum_b ceil(T_b / BLKK) <= tokens / BLKK
-    + batch, and the offsets stay on the device."""
-    batch = cu_seqlens_k.numel() - 1
-    if equal_len is not None:
-        nblk = (equal_len + BLKK - 1) // BLKK
-        cu_scale_i32 = torch.arange(0, (batch + 1) * nblk, nblk, device=k.device, dtype=torch.int32)
-        n_rows = batch * nblk
-    else:
-        _, cu_scale_i32 = _scale_offsets(cu_seqlens_k, BLKK, max_seqlen_k)
-        n_rows = k.shape[0] // BLKK + batch
-    k8 = torch.empty(k.shape, dtype=torch.int8, device=k.device)
-    sk16 = torch.empty((n_rows, k.shape[1]), dtype=torch.float16, device=k.device)
-    cu_i32 = cu_seqlens_k.to(device=k.device, dtype=torch.int32).contiguous()
-    _launch_quant(k, cu_i32, cu_scale_i32, max_seqlen_k, BLKK, 1.0, k8, None, sk16)
-    return k8, sk16, cu_scale_i32
-
-
-@torch.no_grad()
-def _attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q, max_seqlens_k, precision_bitmask, *,
-                       block_m, block_n, block_n_mask, BLKQ, BLKK, causal, sm_scale, mode: str, scalar_scales,
-                       int8_use_fp16_v, bias=None, equal_len: Optional[int] = None, o=None, threshold=None,
-                       k_quant=None):
-    mode_code = _routing_mode_code(mode)
-    int8_path = mode_code != ROUTING_MODE_FP16
-    _check_kernel_support(q, block_m, block_n, BLKK, int8_path, int8_use_fp16_v, bias, max_seqlens_q, max_seqlens_k)
-    if sm_scale is None:
-        sm_scale = q.shape[-1] ** -0.5
-    if o is None:
-        o = torch.empty_like(q)
-    cu_q = cu_seqlens_q.to(device=q.device, dtype=torch.int32).contiguous()
-    cu_k = cu_seqlens_k.to(device=q.device, dtype=torch.int32).contiguous()
-    bm = precision_bitmask.to(device=q.device, dtype=torch.uint64).contiguous()
-    kw = {}
-    if int8_path:
-        if k_quant is not None and equal_len is not None and BLKK == 64:
-            # K codes and fp16 block scales already made (by the RoPE pass), blocks of 64 tokens
-            # per equal-length sequence.
-            k8, sk16 = k_quant
-            nblk = (equal_len + BLKK - 1) // BLKK
-            batch = cu_k.numel() - 1
-            cuks = torch.arange(0, (batch + 1) * nblk, nblk, device=k.device, dtype=torch.int32)
-        else:
-            k8, sk16, cuks = _quantize_k(k, cu_k, max_seqlens_k, BLKK, equal_len)
-        kw = dict(k8=k8, sk=sk16, cuks=cuks)
-        if BLKQ != 128:
-            q8, sq, cuq = per_block_int8_single(q, cu_q, max_seqlens_q, BLK=BLKQ, sm_scale=1.0)
-            kw.update(q8=q8, sq=sq.to(torch.float16).contiguous(), cuqs=cuq.to(torch.int32).contiguous())
-        if not int8_use_fp16_v:
-            # V per BLKK block as K (tilemix.py:45-107): the INT8-V PV path of INT8-routed tiles.
-            # The paired kernel (head_dim 128, block_m 128, Q quantised in kernel, no bias)
-            # reads the codes as exact fp16 values; the general kernel reads the int8 codes.
-            paired = (q.shape[-1] == 128 and block_m == 128 and BLKQ == 128 and bias is None
-                      and BLKK in (64, 128) and not _force_general())
-            if paired:
-                v16, sv16, cuvs = _quantize_v_f16(v, cu_k, max_seqlens_k, BLKK, equal_len)
-                kw.update(v8_f16=v16, sv=sv16, cuvs=cuvs)
-            else:
-                v8, sv16, cuvs = _quantize_k(v, cu_k, max_seqlens_k, BLKK, equal_len)
-                kw.update(v8=v8, sv=sv16, cuvs=cuvs)
-    _launch(q, k, v, o, cu_q, cu_k, bm, max_seqlens_q, max_seqlens_k, block_m=block_m, block_n=block_n,
-            block_n_mask=block_n_mask, BLKQ=BLKQ, BLKK=BLKK, causal=causal, sm_scale=sm_scale,
-            mode_code=mode_code, scalar_scales=scalar_scales, int8_use_fp16_v=int8_use_fp16_v,
-            threshold=threshold, bias=bias, **kw)
-    return o
-
-
-@torch.no_grad()
-def tilemix_attention_with_quant(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q: int, max_seqlens_k: int,
-                                 precision_bitmask, *, block_m: int = 128, block_n: int = 64,
-                                 block_n_mask: Optional[int] = None, BLKQ: int = 128, BLKK: int = 64,
-                                 causal: bool = False, sm_scale: Optional[float] = None,
-                                 bias: Optional[torch.Tensor] = None, routing_mode: RoutingMode = "auto",
-                                 run_length: bool = False, scalar_scales: bool = True, int8_cache_ca: bool = False,
-                                 int8_use_fp16_v: bool = False):
-    """Quantise and run the routed attention (tilemix.py:1340-1447). Returns (out, mode)."""
-    if block_n_mask is None:
-        block_n_mask = block_n
-    normalized_mode = routing_mode.strip().lower()
-    if normalized_mode == "auto":
-        normalized_mode = classify_bitmask_routing(precision_bitmask, seqlen_q=max_seqlens_q,
-                                                   seqlen_k=max_seqlens_k, block_m=block_m, block_n=block_n,
-                                                   block_n_mask=block_n_mask, causal=causal)
-    _validate(q, k, v, max_seqlens_q, max_seqlens_k, precision_bitmask, block_m, block_n, block_n_mask, BLKQ,
-              BLKK, scalar_scales)
-    _routing_mode_code(normalized_mode)
-    o = _attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlens_q, max_seqlens_k, precision_bitmask,
-                           block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, BLKQ=BLKQ, BLKK=BLKK,
-                           causal=causal, sm_scale=sm_scale, mode=normalized_mode, scalar_scales=scalar_scales,
-                           int8_use_fp16_v=int8_use_fp16_v, bias=bias)
-    return o, normalized_mode
-
-
-def _validate(q, k, v, max_q, max_k, bitmask, block_m, block_n, block_n_mask, BLKQ, BLKK, scalar_scales):
-    """The argument checks launch_prequantized performs (tilemix.py:1167-1201)."""
-    if not q.is_cuda:
-        raise RuntimeError("TileMix is a CUDA-only kernel")
-    if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
-        raise ValueError("expected flattened [tokens, heads, dim] tensors")
-    if k.shape != v.shape or q.shape[-1] != k.shape[-1]:
-        raise ValueError("K/V shapes and Q/K/V head dimensions must match")
-    if q.shape[1] % k.shape[1] != 0:
-        raise ValueError("Q heads must be divisible by KV heads")
-    if q.device != k.device or q.device != v.device:
-        raise ValueError("q, k, and v must share one CUDA device")
-    if q.dtype != k.dtype or q.dtype != v.dtype:
-        raise TypeError("q, k, and v must share one dtype")
-    if max_q != max_k:
-        raise ValueError("packed routing currently requires equal Q/K lengths")
-    if block_n_mask % block_n:
-        raise ValueError("block_n_mask must be a multiple of block_n")
-    if (max_k + block_n_mask - 1) // block_n_mask > 64:
-        raise ValueError("packed routing exceeds 64 mask blocks")
-    if scalar_scales and (block_m != BLKQ or block_n != BLKK):
-        raise ValueError("scalar_scales requires block_m == BLKQ and block_n == BLKK")
-    expected_rows = k.shape[1] * ((max_q + block_m - 1) // block_m)
-    if bitmask.dtype != torch.uint64:
-        raise TypeError("precision_bitmask must be torch.uint64")
-    if bitmask.numel() != expected_rows:
-        raise ValueError(f"precision_bitmask has {bitmask.numel()} rows, expected {expected_rows}")
-    if q.shape[-1] > 128:
-        raise ValueError("head dimension must be <= 128")
