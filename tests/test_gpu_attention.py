@@ -19,22 +19,22 @@ MEAN_ABS = 2e-4
 
 
 def _run_case(lens, hq, hk, d, block_m, block_n=64, block_n_mask=64, mode="mixed", causal=True, seed=0,
-              outliers=0, threshold=0.0, bits_seed=1, fp16_v=True, bias_seed=None, return_diff=False):
+              outliers=0, threshold=0.0, bits_seed=1, fp16_v=True, bias_seed=None, return_diff=False, blkk=64):
     from tilemix_b200.attention import tilemix as tmx
 
     q, k, v, cu = make_qkv(lens, hq, hk, d, seed=seed, outliers=outliers)
     T = max(lens)
     rows = hk * ((T + block_m - 1) // block_m)
     bm = random_bitmask(rows, seed=bits_seed)
-    scalar = block_m == 128 and block_n == 64
+    scalar = block_m == 128 and block_n == blkk
     bias = None if bias_seed is None else make_bias(len(lens), hq, T, bias_seed)
     ref = ora.tilemix_attention_with_quant(
         q.numpy(), k.numpy(), v.numpy(), cu.numpy(), cu.numpy(), T, T, bm.numpy().view(np.uint64),
-        block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, causal=causal, routing_mode=mode,
+        block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, BLKK=blkk, causal=causal, routing_mode=mode,
         scalar_scales=scalar, int8_use_fp16_v=fp16_v, bias=None if bias is None else bias.numpy())
     dev = torch.device("cuda", 0)
     out = tmx._attention_forward(q.to(dev), k.to(dev), v.to(dev), cu.to(dev), cu.to(dev), T, T, bm.to(dev),
-                                 block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, BLKQ=128, BLKK=64,
+                                 block_m=block_m, block_n=block_n, block_n_mask=block_n_mask, BLKQ=128, BLKK=blkk,
                                  causal=causal, sm_scale=None, mode=mode, scalar_scales=scalar,
                                  int8_use_fp16_v=fp16_v, threshold=threshold,
                                  bias=None if bias is None else bias.to(dev))
@@ -105,6 +105,14 @@ V8_CASES = [
 @pytest.mark.parametrize("threshold", [0.0, 8.0, 15.0])
 def test_attention_int8_v_path_matches_oracle(cuda_device, lens, hq, hk, d, block_m, bnm, mode, threshold):
     mx, mean = _run_case(lens, hq, hk, d, block_m, 64, bnm, mode, threshold=threshold, fp16_v=False, seed=3)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.parametrize("fp16_v", [True, False])
+def test_attention_blkk_128_matches_oracle(cuda_device, fp16_v):
+    """K (and V) scale blocks of 128 keys: two 64-key tiles per scale row, tracked by the
+    paired kernel's step loop (per-key scale vectors in the reference, scalar_scales off)."""
+    mx, mean = _run_case([1024, 640], 6, 2, 128, 128, 64, 64, "mixed", fp16_v=fp16_v, seed=4, blkk=128)
     assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
 
 
