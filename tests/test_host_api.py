@@ -164,3 +164,51 @@ def test_validate_order_and_messages(change, exc, text):
     args.update(change)
     with pytest.raises(exc, match=text):
         _validate(**args)
+
+
+def _int8_v_params(**over):
+    """tm_attn_params of an INT8-routed INT8-V call with stand-in (aligned, never read) pointers."""
+    from tilemix_b200._lib import TmAttnParams
+
+    p = TmAttnParams()
+    fake = 0x100000
+    for name in ("q", "k", "v", "out", "cu_seqlens_q", "cu_seqlens_k", "k8", "k_scale", "cu_k_scale", "v8",
+                 "v_scale", "cu_v_scale"):
+        setattr(p, name, fake)
+    p.q_stride_tok, p.q_stride_head = 8 * 128, 128
+    p.k_stride_tok, p.k_stride_head = 8 * 128, 128
+    p.v_stride_tok, p.v_stride_head = 8 * 128, 128
+    p.o_stride_tok, p.o_stride_head = 8 * 128, 128
+    p.k8_stride_tok, p.k8_stride_head = 8 * 128, 128
+    p.v8_stride_tok, p.v8_stride_head = 8 * 128, 128
+    p.q_tokens = p.k_tokens = 256
+    p.batch, p.heads_q, p.heads_k, p.head_dim = 0, 8, 8, 128
+    p.max_seqlen_q = p.max_seqlen_k = 256
+    p.block_m, p.block_n, p.block_n_mask, p.blkq, p.blkk = 128, 64, 64, 128, 64
+    p.routing_mode, p.int8_use_fp16_v, p.sm_scale = 2, 0, 0.088
+    for k, v in over.items():
+        setattr(p, k, v)
+    return p
+
+
+def test_int8_v_operand_rules_need_no_gpu():
+    """INT8-V takes the int8 V codes (any kernel) or their fp16 copy (the paired kernel's shape:
+    head_dim 128, block_m 128, Q quantised in the kernel, no bias, automatic kernel choice)."""
+    from tilemix_b200._lib import TmAttnTuning, lib
+
+    def rc(p, force_general=0):
+        t = TmAttnTuning()
+        t.force_general = force_general
+        return lib().tm_attn_fwd_ex(ctypes.byref(p), ctypes.byref(t), None)
+
+    fake = 0x200000
+    assert rc(_int8_v_params()) == 0                                    # int8 codes, empty batch
+    assert rc(_int8_v_params(v8=None)) == -1                            # neither operand
+    assert rc(_int8_v_params(v8=None, v8_f16=fake, v8_f16_stride_tok=1024, v8_f16_stride_head=128)) == 0
+    assert rc(_int8_v_params(v8=None, v8_f16=fake), force_general=1) == -1             # general kernel
+    assert rc(_int8_v_params(v8=None, v8_f16=fake, head_dim=64, q_stride_head=64)) == -1  # not the paired shape
+    assert rc(_int8_v_params(v8=None, v8_f16=fake, q8=fake, q_scale=fake, cu_q_scale=fake)) == -1  # prequantised Q
+    assert rc(_int8_v_params(v_scale=None)) == -1                       # V scales
+    # a misaligned fp16 copy is rejected before anything runs (non-empty batch)
+    assert rc(_int8_v_params(batch=1, v8=None, v8_f16=fake + 8, v8_f16_stride_tok=1024,
+                             v8_f16_stride_head=128)) == -3
