@@ -169,3 +169,31 @@ def test_from_host_entry_point_matches_device_call(cuda_device, chunk, ring):
                                        device=dev, chunk_seqs=chunk, ring=ring)
     torch.cuda.synchronize()
     assert torch.equal(out, ref.permute(0, 2, 1, 3).reshape(B * T, hq, d).cpu())
+
+
+@pytest.mark.parametrize("fp16_v,mode", [(True, "mixed"), (False, "mixed"), (False, "auto")])
+def test_launch_prequantized_matches_oracle(cuda_device, fp16_v, mode):
+    """launch_prequantized (tilemix.py:1132-1336) on codes from quantize_qkv_for_tilemix: the
+    general kernel's prequantised-Q path, INT8-V from the int8 V codes, and the routing mode
+    returned as the reference does ("auto" classifies the map)."""
+    from tilemix_b200.attention.tilemix import launch_prequantized, quantize_qkv_for_tilemix
+
+    lens, hq, hk, d = [640, 300, 512], 4, 2, 128
+    T = max(lens)
+    q, k, v, cu = make_qkv(lens, hq, hk, d, seed=6)
+    bm = random_bitmask(hk * ((T + 127) // 128), seed=3)
+    ref = ora.tilemix_attention_with_quant(
+        q.numpy(), k.numpy(), v.numpy(), cu.numpy(), cu.numpy(), T, T, bm.numpy().view(np.uint64), block_m=128,
+        block_n=64, block_n_mask=64, causal=True, routing_mode="mixed", scalar_scales=False,
+        int8_use_fp16_v=fp16_v)
+    dev = cuda_device
+    qd, kd, vd, cud = q.to(dev), k.to(dev), v.to(dev), cu.to(dev)
+    q8, sq, cuq, k8, sk, cuk, v8, sv, cuv = quantize_qkv_for_tilemix(qd, kd, vd, cud, cud, T, T, BLKQ=128, BLKK=64)
+    out, got_mode = launch_prequantized(qd, kd, vd, cud, cud, T, T, bm.to(dev), q8=q8, k8=k8, v8=v8, sQ_blocks=sq,
+                                        sK_blocks=sk, sV_blocks=sv, cu_q_scale=cuq, cu_k_scale=cuk, cu_v_scale=cuv,
+                                        block_m=128, block_n=64, block_n_mask=64, BLKQ=128, BLKK=64, causal=True,
+                                        routing_mode=mode, scalar_scales=False, int8_use_fp16_v=fp16_v)
+    torch.cuda.synchronize()
+    assert got_mode == "mixed"
+    mx, mean = err_stats(out, ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
