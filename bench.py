@@ -513,14 +513,18 @@ def run_ours(args) -> None:
         def step(evs=None):
             for i, p in enumerate(probs):
                 k8 = sk16 = cuks = None
+                vkw = {}
                 if mode_code != tmx.ROUTING_MODE_FP16:
                     k8, sk16, cuks = tmx._quantize_k(p["k"], p["cu"], p["T"], 64, equal_len=p["T"])
+                    if args.int8_v:  # the API default's V path: V quantised, its codes as fp16 values
+                        v16, sv16, cuvs = tmx._quantize_v_f16(p["v"], p["cu"], p["T"], 64, equal_len=p["T"])
+                        vkw = dict(v8_f16=v16, sv=sv16, cuvs=cuvs)
                 if evs is not None:
                     evs[i][0].record()
                 tmx._launch(p["q"], p["k"], p["v"], p["o"], p["cu"], p["cu"], p[pm_key], p["T"], p["T"], k8=k8,
                             sk=sk16, cuks=cuks, block_m=bm, block_n=bn, block_n_mask=bnm, BLKQ=128, BLKK=64,
                             causal=True, sm_scale=sm_scale, mode_code=mode_code, scalar_scales=True,
-                            int8_use_fp16_v=True, threshold=thr)
+                            int8_use_fp16_v=not args.int8_v, threshold=thr, **vkw)
                 if evs is not None:
                     evs[i][1].record()
         return step
@@ -640,7 +644,7 @@ def run_ours(args) -> None:
     achieved = rank_flops / (attn_ms * 1e-3) / 1e12
     t_star_ms = (rank_flops / 2 * (1 - share) / peak16 + rank_flops / 2 * share / peak8 + rank_flops / 2 / peak16) \
         / 1e12 * 1e3
-    traffic = profiled_traffic("attn_fwd_paired_config2")
+    traffic = profiled_traffic("attn_fwd_paired_int8v_config2" if args.int8_v else "attn_fwd_paired_config2")
     if traffic is not None and world > 1:
         traffic = int(traffic * rank_flops / total_flops)
 
@@ -669,7 +673,9 @@ def run_ours(args) -> None:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp16+int8", "data": "synthetic (seeded N(0,1) with outlier channels)",
-            "config": config_dict(world, shard_desc),
+            "config": {**config_dict(world, shard_desc),
+                       "v_path": ("INT8-V (int8_use_fp16_v=False): the step also quantises V" if args.int8_v
+                                  else "FP16 V for INT8 tiles (int8_use_fp16_v=True)")},
             "roofline": {
                 "bound": "tensor", "kernel": "attn_fwd_paired", "achieved": achieved,
                 "peak": rank_flops / t_star_ms / 1e9, "unit": "TFLOP/s", "frac": t_star_ms / attn_ms,
@@ -690,7 +696,7 @@ def run_ours(args) -> None:
                            "1 sequence per chunk)"},
             "scatter_ms": scatter_ms,
             "clocks": clocks,
-            "gpu_launches": 2 * len(problems) * args.steps,
+            "gpu_launches": (3 if args.int8_v else 2) * len(problems) * args.steps,
             "rescale_threshold": thr,
             "numerics": tmx.numerics_mode(),
         }
@@ -1038,6 +1044,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the oracle timing on the host cores")
+    ap.add_argument("--int8-v", action="store_true",
+                    help="INT8-routed tiles take the INT8-V PV path (int8_use_fp16_v=False, the API's default): "
+                         "the step also quantises V")
     ap.add_argument("--no-triton-reference", action="store_true",
                     help="skip timing the reference's Triton kernels on the GPU (N=1 line)")
     ap.add_argument("--batch", type=int, default=CFG["batch"],
