@@ -241,8 +241,9 @@ int tm_attn_fwd_ex(const tm_attn_params* params, const tm_attn_tuning* tuning, v
  * argument is checked before anything is queued. params->k8, k_scale and
  * cu_k_scale must be NULL. FP16-only routing needs no K operand and forwards
  * to tm_attn_fwd_ex. The INT8-V PV path (int8_use_fp16_v == 0 with an INT8
- * route) still reads v8 / v_scale / cu_v_scale from the caller: callers that
- * pass only Q/K/V/O set int8_use_fp16_v = 1. The call allocates nothing. Its
+ * route) still reads its V operand (v8, or v8_f16 for the paired kernel's
+ * shape) and v_scale / cu_v_scale from the caller: callers that pass only
+ * Q/K/V/O set int8_use_fp16_v = 1. The call allocates nothing. Its
  * first call on a device resolves the scratch address (a runtime query, which
  * can fail with TM_ERR_LAUNCH if the module cannot be loaded there), so make a
  * warm-up call at initialisation, before any stream capture. Calls that may
