@@ -197,3 +197,15 @@ def test_launch_prequantized_matches_oracle(cuda_device, fp16_v, mode):
     assert got_mode == "mixed"
     mx, mean = err_stats(out, ref)
     assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.parametrize("lens,d,block_m,fp16_v", [
+    ([512, 0, 300], 128, 128, True),      # paired kernel: the empty sequence's units are skipped
+    ([512, 0, 300], 128, 128, False),     # paired kernel, INT8-V
+    ([200, 0, 0, 130], 64, 64, False),    # general kernel
+])
+def test_zero_length_sequences_match_oracle(cuda_device, lens, d, block_m, fp16_v):
+    """Empty sequences inside a varlen batch (cu_seqlens with equal neighbours): no rows,
+    no K scale blocks, and the other sequences' outputs as the oracle's."""
+    mx, mean = _run_case(lens, 4, 2, d, block_m, 64, 64, "mixed", fp16_v=fp16_v, seed=2)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)

@@ -11,7 +11,8 @@ pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("exact_numerics")]
 
 
 @pytest.mark.parametrize("lens,h,d,blk", [([512], 4, 64, 128), ([4096, 1000, 1], 8, 128, 64),
-                                          ([300, 129], 3, 128, 128), ([64], 1, 64, 256)])
+                                          ([300, 129], 3, 128, 128), ([64], 1, 64, 256),
+                                          ([300, 0, 129], 3, 128, 64)])
 def test_quant_bit_exact(cuda_device, lens, h, d, blk):
     from tilemix_b200.attention.quant_per_block_varlen import per_block_int8_single
 
